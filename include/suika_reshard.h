@@ -1,0 +1,249 @@
+/*
+ * suika_reshard.h -- C ABI of the B200 live-reshard path.
+ *
+ * This library replaces the data path of Suika's live state migration:
+ *   schedule_param_transfer           Suika/migration.py:322-381  -> rs_plan_build / rs_plan_get_ops
+ *   execute_param_transfer            Suika/migration.py:397-556  -> rs_program_build + rs_copy_launch
+ *   schedule_and_execute_param_transfer Suika/migration.py:558-598 (the Python mirror in
+ *                                     suika_b200/migration.py drives the calls below)
+ *   TensorMeta / ParamLayout          Suika/migration.py:29-131, 161-254 -> rs_tensor_meta / rs_rank_layout
+ *   TransferOp                        Suika/migration.py:257-312 -> rs_op
+ *   dist.isend/irecv per tensor       Suika/utils.py:212-236 -> peer pull through rs_peer_open + rs_copy_launch
+ *
+ * Conventions
+ *   - Every function returns an int status: RS_OK (0) or a negative rs_status code.
+ *     rs_last_error() returns a message for the last failure on the calling thread.
+ *   - No C++ exception crosses this boundary.
+ *   - Plans and programs are immutable after build and may be shared between threads;
+ *     no global mutable state survives a call except the per-thread error message.
+ *   - Pointers named *_dev are device addresses; everything else is host memory.
+ */
+#ifndef SUIKA_RESHARD_H
+#define SUIKA_RESHARD_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define RS_MAX_DIMS 8
+/* slice_dim value meaning "tp_meta is None" (tensor replicated across TP). */
+#define RS_NO_SLICE (-1000)
+
+enum rs_status {
+  RS_OK = 0,
+  RS_ERR_ARG = -1,          /* bad argument / malformed descriptor                         */
+  RS_ERR_NO_OWNER = -2,     /* "illegal transfer": a target piece has no owner (migration.py:356) */
+  RS_ERR_SHAPE = -3,        /* shape / divisibility mismatch (migration.py:293-294,311)      */
+  RS_ERR_SLICE_DIM = -4,    /* slice dim mismatch between source and target (migration.py:294, 229) */
+  RS_ERR_EMPTY_SOURCE = -5, /* source layout holds no tensor (max() of empty, migration.py:335) */
+  RS_ERR_CUDA = -6,         /* a CUDA runtime call failed                                   */
+  RS_ERR_BOUNDS = -7,       /* a copy would leave the extent of its source or target        */
+  RS_ERR_CAPACITY = -8,     /* caller buffer or workspace too small                         */
+  RS_ERR_PEER = -9,         /* peer memory export / import failed                           */
+  RS_ERR_SUBFIELD = -10     /* sub-field list inconsistent (migration.py:441)               */
+};
+
+/* Cat order of a target tensor assembled from several pieces. */
+enum rs_order {
+  /* Reproduce the reference: remote pieces in op order, then self pieces in op order
+   * (remote pieces are appended while ops are issued, migration.py:472-492; self pieces by the
+   * deferred closures, migration.py:448-459 run at :508-509; torch.cat at :536). */
+  RS_ORDER_REFERENCE = 0,
+  /* Pieces in slice order: the target equals the re-slice of the full tensor. */
+  RS_ORDER_SEMANTIC = 1
+};
+
+/* Source choice among the owners of a target piece. */
+enum rs_src_choice {
+  RS_SRC_REFERENCE = 0, /* the reference's greedy rule, migration.py:355-379 */
+  RS_SRC_BALANCED = 1   /* least loaded owner by egress bytes, then by rank  */
+};
+
+/* One TensorMeta (migration.py:29-131): full (unsharded) shape and TP slicing. */
+typedef struct rs_tensor_meta {
+  int32_t name_id;              /* index into the caller's name table (shared by all layouts) */
+  int32_t ndim;
+  int64_t shape[RS_MAX_DIMS];   /* FULL shape: TensorMeta.shape                               */
+  int32_t itemsize;             /* bytes per element of TensorMeta.dtype                       */
+  int32_t slice_dim;            /* tp_meta[0], or RS_NO_SLICE when tp_meta is None             */
+  int32_t tp_index;             /* tp_meta[1]                                                  */
+  int32_t tp_deg;               /* tp_meta[2]                                                  */
+} rs_tensor_meta;
+
+/* One entry of ParamLayout.layout (migration.py:161-170): rank -> {name -> meta},
+ * tensors in the dict's iteration order. Layout arrays list ranks in dict order too. */
+typedef struct rs_rank_layout {
+  int32_t rank;
+  int32_t n_tensors;
+  const rs_tensor_meta* tensors;
+} rs_rank_layout;
+
+typedef struct rs_plan_opts {
+  int32_t minimum_est_peers; /* 1 if IB is enabled else 2 (migration.py:340, utils.py:209-210) */
+  int32_t order;             /* enum rs_order                                                  */
+  int32_t src_choice;        /* enum rs_src_choice                                             */
+  int32_t reserved;
+} rs_plan_opts;
+
+/* One TransferOp (migration.py:257-312). The target piece is the rescaled target meta
+ * (scale_to_tp, migration.py:103-118); tp fields use RS_NO_SLICE when tp_meta is None. */
+typedef struct rs_op {
+  int32_t name_id;
+  int32_t src_rank;
+  int32_t dst_rank;
+  int32_t src_slice_dim, src_tp_index, src_tp_deg;
+  int32_t dst_slice_dim, dst_tp_index, dst_tp_deg;
+  int32_t reserved;
+  int64_t numel;               /* elements of the target piece (TensorMeta.numel())            */
+} rs_op;
+
+typedef struct rs_plan rs_plan;
+typedef struct rs_program rs_program;
+
+const char* rs_last_error(void);
+int rs_version(int32_t* major, int32_t* minor);
+
+/* ---- planning: schedule_param_transfer (migration.py:322-381) -------------------------- */
+int rs_plan_build(const rs_rank_layout* src, int32_t n_src,
+                  const rs_rank_layout* dst, int32_t n_dst,
+                  const rs_plan_opts* opts, rs_plan** out);
+int rs_plan_num_ops(const rs_plan* plan, int64_t* n_ops);
+int rs_plan_get_ops(const rs_plan* plan, rs_op* ops, int64_t capacity);
+void rs_plan_free(rs_plan* plan);
+
+/* ---- per-rank program: the op loop + post-process of execute_param_transfer --------------
+ * (migration.py:426-545). For one executing rank it lists the tensors the rank must produce
+ * (dst slots), the source tensors it reads (src slots, local or on a peer), the meta
+ * (singleton) sub-fields it fills, and the strided copies ("segments") that build every dst
+ * slot in place: a TP-grow chunk (get_send_tensor, migration.py:290-312) becomes a row-strided
+ * read, a TP-shrink concat (torch.cat, migration.py:536) becomes a row-strided write. */
+
+/* One entry of other_context_dict["expected_sub_fields"] (migration.py:702-709). */
+typedef struct rs_subfield {
+  int32_t itemsize;   /* bytes per element of this sub-field's tensors          */
+  int32_t is_meta;    /* 1: singleton "meta" field (e.g. Adam step), 0: "normal" */
+} rs_subfield;
+
+typedef struct rs_program_counts {
+  int64_t n_dst_slots;
+  int64_t n_src_slots;
+  int64_t n_meta_slots;
+  int64_t n_segments;
+  uint64_t remote_bytes;   /* bytes this rank reads from other ranks           */
+  uint64_t local_bytes;    /* bytes this rank copies from its own sources       */
+} rs_program_counts;
+
+/* A target tensor to allocate: target_state_dict[name][sub_field]. */
+typedef struct rs_dst_slot {
+  int32_t name_id;
+  int32_t subfield;
+  int32_t ndim;
+  int32_t reserved;
+  int64_t shape[RS_MAX_DIMS];  /* actual (sharded) shape of the target, migration.py:92-98 */
+  uint64_t nbytes;
+} rs_dst_slot;
+
+/* A source tensor read by this rank: source_state_dict[name][sub_field] on src_rank. */
+typedef struct rs_src_slot {
+  int32_t src_rank;
+  int32_t name_id;
+  int32_t subfield;
+  int32_t reserved;
+  uint64_t nbytes;             /* bytes the source tensor must hold */
+} rs_src_slot;
+
+/* A singleton sub-field of a target tensor: its value is the one of the first piece in cat
+ * order (tensors[0].clone(), migration.py:538). first_is_self tells which shape the reference
+ * gives it: the source tensor's own shape when the first piece is a self transfer
+ * (migration.py:446), shape [1] when it was received (migration.py:486-487). */
+typedef struct rs_meta_slot {
+  int32_t name_id;
+  int32_t subfield;
+  int32_t src_rank;
+  int32_t first_is_self;
+} rs_meta_slot;
+
+/* One strided copy: rows x row_bytes from src slot (offset, pitch) to dst slot (offset, pitch). */
+typedef struct rs_segment {
+  int32_t src_slot;
+  int32_t dst_slot;
+  uint64_t src_offset;
+  uint64_t dst_offset;
+  uint64_t rows;
+  uint64_t row_bytes;
+  uint64_t src_pitch;
+  uint64_t dst_pitch;
+} rs_segment;
+
+int rs_program_build(const rs_plan* plan, int32_t rank,
+                     const rs_subfield* subfields, int32_t n_subfields,
+                     rs_program** out);
+int rs_program_counts_get(const rs_program* prog, rs_program_counts* out);
+int rs_program_dst_slots(const rs_program* prog, rs_dst_slot* out, int64_t capacity);
+int rs_program_src_slots(const rs_program* prog, rs_src_slot* out, int64_t capacity);
+int rs_program_meta_slots(const rs_program* prog, rs_meta_slot* out, int64_t capacity);
+int rs_program_segments(const rs_program* prog, rs_segment* out, int64_t capacity);
+void rs_program_free(rs_program* prog);
+
+/* Absolute copy descriptor consumed by the device kernel. */
+typedef struct rs_copy_desc {
+  uint64_t src_dev;
+  uint64_t dst_dev;
+  uint64_t rows;
+  uint64_t row_bytes;
+  uint64_t src_pitch;
+  uint64_t dst_pitch;
+} rs_copy_desc;
+
+/* Bind the program's slots to addresses. src_dev[i]/src_extent[i]: address of src slot i and
+ * the bytes readable from it; same for dst. Every segment is checked against the extents
+ * (RS_ERR_BOUNDS) before it is written to out[]. Writes rs_program_counts.n_segments entries. */
+int rs_program_resolve(const rs_program* prog,
+                       const uint64_t* src_dev, const uint64_t* src_extent,
+                       const uint64_t* dst_dev, const uint64_t* dst_extent,
+                       rs_copy_desc* out, int64_t capacity);
+
+/* ---- device execution (sm_100a) ----------------------------------------------------------
+ * One launch executes a whole copy table: local HBM copies and pulls from peer HBM over
+ * NVLink alike (a peer address comes from rs_peer_open). Replaces the per-tensor
+ * isend/irecv + contiguous/cat/clone of migration.py:466,489,501,536-538. */
+
+typedef struct rs_launch_info {
+  uint64_t n_tiles;        /* work units the table was cut into */
+  uint64_t total_bytes;    /* bytes copied                      */
+  int32_t grid;            /* CTAs launched                     */
+  int32_t block;           /* threads per CTA                   */
+} rs_launch_info;
+
+/* Device workspace the caller must provide to rs_copy_launch for n descriptors. */
+int rs_copy_workspace_bytes(int64_t n_desc, uint64_t* bytes);
+/* Stage the table into workspace_dev (stream-ordered) and launch the copy kernel on stream
+ * (a cudaStream_t; NULL = legacy default stream). Asynchronous: synchronise the stream
+ * before reading the targets. n_desc == 0 is a no-op. */
+int rs_copy_launch(const rs_copy_desc* descs, int64_t n_desc,
+                   void* workspace_dev, uint64_t workspace_bytes,
+                   void* stream, rs_launch_info* info);
+
+/* ---- peer memory (replaces NCCL P2P connections, utils.py:212-236) ----------------------- */
+typedef struct rs_peer_handle {
+  uint8_t ipc[64];          /* cudaIpcMemHandle_t of the allocation      */
+  uint64_t alloc_base;      /* exporter's base address of the allocation */
+  uint64_t alloc_bytes;     /* size of the allocation                    */
+  int32_t device;           /* exporter's device ordinal                 */
+  int32_t pid;              /* exporter's process id                     */
+} rs_peer_handle;
+
+/* Export the allocation that contains ptr_dev; *offset = ptr_dev - allocation base. */
+int rs_peer_export(const void* ptr_dev, rs_peer_handle* out, uint64_t* offset);
+/* Map a peer's exported allocation into this process (current device); *base_dev is the
+ * local address of the allocation base. Close with rs_peer_close after every reader is done. */
+int rs_peer_open(const rs_peer_handle* handle, void** base_dev);
+int rs_peer_close(void* base_dev);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SUIKA_RESHARD_H */

@@ -1,0 +1,333 @@
+// Device executor of the B200 live-reshard path (sm_100a), C ABI in include/suika_reshard.h.
+//
+// One launch runs a whole copy table for one target rank. Each entry is a strided copy
+// (rows x row_bytes, independent source and target pitches) whose source is either this GPU's
+// HBM or a peer GPU's HBM mapped through CUDA IPC, so a single kernel does what the reference
+// spreads over per-tensor NCCL isend/irecv, chunk().contiguous() and torch.cat/clone
+// (Suika/migration.py:310,466,489,501,536-538; Suika/utils.py:212-236).
+//
+// Work decomposition: every entry is cut into tiles of about kTileBytes (whole rows when rows
+// are short, column chunks of one row when rows are long); the tile list is implicit (a prefix
+// of tile counts per entry, binary-searched by each CTA). CTAs stride over tiles; a CTA moves a
+// tile with 16-byte vector loads/stores (narrower only when an address or pitch is not 16-byte
+// aligned), several loads in flight per thread before their stores, which keeps enough bytes
+// outstanding to cover NVLink read latency as well as HBM latency. The copy is pure data
+// movement: no tensor cores, no TMA multicast (this code runs on several GPUs), no waits.
+#include "../../include/suika_reshard.h"
+#include "internal.h"
+
+#include <cuda_runtime.h>
+#include <cuda.h>
+
+#include <algorithm>
+#include <cstdlib>
+#include <cstring>
+#include <string>
+#include <unistd.h>
+#include <vector>
+
+namespace {
+
+int efail(int code, const std::string& msg) { return suika_rs::fail(code, msg); }
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return efail(RS_ERR_CUDA, std::string(what) + ": " + cudaGetErrorName(e) + " (" + cudaGetErrorString(e) + ")");
+}
+
+// One table entry as the kernel reads it (72 bytes).
+struct DevSeg {
+  uint64_t src;
+  uint64_t dst;
+  uint64_t src_pitch;
+  uint64_t dst_pitch;
+  uint64_t tile_begin;   // global index of this entry's first tile
+  uint64_t row_bytes;
+  uint64_t col_bytes;    // bytes of one column chunk when rows are split, else row_bytes
+  uint32_t rows;
+  uint32_t rows_per_tile;
+  uint32_t col_tiles;    // column chunks per row (1 when whole rows fit in a tile)
+  uint32_t vshift;       // log2 of the vector width (0..4)
+};
+static_assert(sizeof(DevSeg) == 72, "DevSeg layout");
+
+constexpr int kBlock = 512;
+constexpr uint64_t kDefaultTileBytes = 128 * 1024;
+
+template <int VB> struct Vec;
+template <> struct Vec<16> { using T = uint4; };
+template <> struct Vec<8> { using T = uint2; };
+template <> struct Vec<4> { using T = uint32_t; };
+template <> struct Vec<2> { using T = uint16_t; };
+template <> struct Vec<1> { using T = uint8_t; };
+
+// Source reads bypass L1 allocation (each byte is read once); the source is not written while
+// the kernel runs.
+__device__ __forceinline__ uint4 load_vec(const uint4* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ uint2 load_vec(const uint2* p) {
+  uint2 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ uint32_t load_vec(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ uint16_t load_vec(const uint16_t* p) { return __ldg(reinterpret_cast<const unsigned short*>(p)); }
+__device__ __forceinline__ uint8_t load_vec(const uint8_t* p) { return __ldg(reinterpret_cast<const unsigned char*>(p)); }
+
+__device__ __forceinline__ void store_vec(uint4* p, const uint4& v) {
+  asm volatile("st.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w) : "memory");
+}
+__device__ __forceinline__ void store_vec(uint2* p, const uint2& v) {
+  asm volatile("st.global.v2.u32 [%0], {%1,%2};" ::"l"(p), "r"(v.x), "r"(v.y) : "memory");
+}
+__device__ __forceinline__ void store_vec(uint32_t* p, const uint32_t& v) { *p = v; }
+__device__ __forceinline__ void store_vec(uint16_t* p, const uint16_t& v) { *p = v; }
+__device__ __forceinline__ void store_vec(uint8_t* p, const uint8_t& v) { *p = v; }
+
+// Copy an nr x (vpr * VB bytes) rectangle. U loads are issued before their stores.
+template <int VB, int U>
+__device__ __forceinline__ void copy_rect(const char* __restrict__ src, char* __restrict__ dst, uint32_t nr,
+                                          uint32_t vpr, uint64_t sp, uint64_t dp) {
+  using V = typename Vec<VB>::T;
+  const uint32_t total = nr * vpr;
+  const uint32_t stride = blockDim.x;
+  if (nr == 1) {
+    const V* s = reinterpret_cast<const V*>(src);
+    V* d = reinterpret_cast<V*>(dst);
+    for (uint32_t base = threadIdx.x; base < total; base += stride * U) {
+      V v[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const uint32_t i = base + u * stride;
+        if (i < total) v[u] = load_vec(s + i);
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const uint32_t i = base + u * stride;
+        if (i < total) store_vec(d + i, v[u]);
+      }
+    }
+    return;
+  }
+  for (uint32_t base = threadIdx.x; base < total; base += stride * U) {
+    V v[U];
+    uint64_t doff[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const uint32_t i = base + u * stride;
+      if (i < total) {
+        const uint32_t r = i / vpr;
+        const uint32_t c = i - r * vpr;
+        v[u] = load_vec(reinterpret_cast<const V*>(src + r * sp + (uint64_t)c * VB));
+        doff[u] = r * dp + (uint64_t)c * VB;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const uint32_t i = base + u * stride;
+      if (i < total) store_vec(reinterpret_cast<V*>(dst + doff[u]), v[u]);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kBlock) rs_copy_kernel(const DevSeg* __restrict__ segs, int32_t nseg, uint64_t ntiles) {
+  for (uint64_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
+    // Entry owning tile t: the last one whose tile_begin <= t.
+    int32_t lo = 0, hi = nseg - 1;
+    while (lo < hi) {
+      const int32_t mid = (lo + hi + 1) >> 1;
+      if (segs[mid].tile_begin <= t) lo = mid; else hi = mid - 1;
+    }
+    const DevSeg s = segs[lo];
+    const uint64_t lt = t - s.tile_begin;
+    const uint64_t rg = lt / s.col_tiles;
+    const uint64_t col = lt - rg * s.col_tiles;
+    const uint64_t r0 = rg * s.rows_per_tile;
+    const uint32_t nr = (uint32_t)min((uint64_t)s.rows_per_tile, (uint64_t)s.rows - r0);
+    const uint64_t c0 = col * s.col_bytes;
+    const uint64_t nb = min(s.col_bytes, s.row_bytes - c0);
+    const char* src = reinterpret_cast<const char*>(s.src) + r0 * s.src_pitch + c0;
+    char* dst = reinterpret_cast<char*>(s.dst) + r0 * s.dst_pitch + c0;
+    const uint32_t vpr = (uint32_t)(nb >> s.vshift);
+    switch (s.vshift) {
+      case 4: copy_rect<16, 4>(src, dst, nr, vpr, s.src_pitch, s.dst_pitch); break;
+      // Narrow widths only serve entries whose addresses or pitches are not 16-byte aligned
+      // (odd shapes); one load in flight per thread keeps their register cost off the main path.
+      case 3: copy_rect<8, 1>(src, dst, nr, vpr, s.src_pitch, s.dst_pitch); break;
+      case 2: copy_rect<4, 1>(src, dst, nr, vpr, s.src_pitch, s.dst_pitch); break;
+      case 1: copy_rect<2, 1>(src, dst, nr, vpr, s.src_pitch, s.dst_pitch); break;
+      default: copy_rect<1, 1>(src, dst, nr, vpr, s.src_pitch, s.dst_pitch); break;
+    }
+  }
+}
+
+uint64_t env_u64(const char* name, uint64_t dflt) {
+  const char* v = std::getenv(name);
+  if (!v || !*v) return dflt;
+  char* end = nullptr;
+  const unsigned long long x = std::strtoull(v, &end, 10);
+  return (end && *end == 0 && x > 0) ? (uint64_t)x : dflt;
+}
+
+// Largest power of two <= 16 dividing every address, pitch and row length of the entry.
+uint32_t vector_shift(const rs_copy_desc& d) {
+  const uint64_t bits = d.src_dev | d.dst_dev | d.row_bytes | (d.rows > 1 ? (d.src_pitch | d.dst_pitch) : 0);
+  uint32_t s = 4;
+  while (s > 0 && (bits & ((1ull << s) - 1))) --s;
+  return s;
+}
+
+}  // namespace
+
+extern "C" {
+
+int rs_copy_workspace_bytes(int64_t n_desc, uint64_t* bytes) {
+  if (!bytes || n_desc < 0) return efail(RS_ERR_ARG, "rs_copy_workspace_bytes: bad argument");
+  *bytes = ((uint64_t)n_desc * sizeof(DevSeg) + 255) & ~255ull;
+  return RS_OK;
+}
+
+int rs_copy_launch(const rs_copy_desc* descs, int64_t n_desc, void* workspace_dev, uint64_t workspace_bytes, void* stream,
+                   rs_launch_info* info) {
+  if (info) std::memset(info, 0, sizeof(*info));
+  if (n_desc < 0 || (n_desc > 0 && !descs)) return efail(RS_ERR_ARG, "rs_copy_launch: bad descriptor array");
+  const uint64_t tile_bytes = std::min<uint64_t>(1ull << 30, std::max<uint64_t>(256, env_u64("SUIKA_RS_TILE_BYTES", kDefaultTileBytes))) & ~15ull;
+  std::vector<DevSeg> table;
+  table.reserve((size_t)n_desc);
+  uint64_t ntiles = 0, total = 0;
+  for (int64_t i = 0; i < n_desc; ++i) {
+    const rs_copy_desc& d = descs[i];
+    if (d.rows == 0 || d.row_bytes == 0) continue;
+    if (d.rows > 0xffffffffull) return efail(RS_ERR_ARG, "rs_copy_launch: entry " + std::to_string(i) + " has more than 2^32 rows");
+    if (d.rows > 1 && (d.row_bytes > d.src_pitch || d.row_bytes > d.dst_pitch))
+      return efail(RS_ERR_ARG, "rs_copy_launch: entry " + std::to_string(i) + " has rows longer than their pitch");
+    if (!d.src_dev || !d.dst_dev) return efail(RS_ERR_ARG, "rs_copy_launch: entry " + std::to_string(i) + " has a NULL address");
+    DevSeg s;
+    s.src = d.src_dev;
+    s.dst = d.dst_dev;
+    s.src_pitch = d.src_pitch;
+    s.dst_pitch = d.dst_pitch;
+    s.rows = (uint32_t)d.rows;
+    s.row_bytes = d.row_bytes;
+    s.vshift = vector_shift(d);
+    s.tile_begin = ntiles;
+    if (d.row_bytes >= tile_bytes) {
+      s.col_bytes = tile_bytes;
+      s.col_tiles = (uint32_t)((d.row_bytes + tile_bytes - 1) / tile_bytes);
+      s.rows_per_tile = 1;
+      ntiles += (uint64_t)s.col_tiles * d.rows;
+    } else {
+      s.col_bytes = d.row_bytes;
+      s.col_tiles = 1;
+      s.rows_per_tile = (uint32_t)std::max<uint64_t>(1, tile_bytes / d.row_bytes);
+      ntiles += (d.rows + s.rows_per_tile - 1) / s.rows_per_tile;
+    }
+    total += d.rows * d.row_bytes;
+    table.push_back(s);
+  }
+  if (table.empty()) return RS_OK;
+  if (table.size() > 0x7fffffffull) return efail(RS_ERR_ARG, "rs_copy_launch: too many entries");
+  const uint64_t need = ((uint64_t)table.size() * sizeof(DevSeg) + 255) & ~255ull;
+  if (!workspace_dev || workspace_bytes < need)
+    return efail(RS_ERR_CAPACITY, "rs_copy_launch: workspace of " + std::to_string(workspace_bytes) + " bytes, need " + std::to_string(need));
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemcpyAsync(workspace_dev, table.data(), table.size() * sizeof(DevSeg), cudaMemcpyHostToDevice, st);
+  if (e != cudaSuccess) return cuda_fail(e, "rs_copy_launch: staging the copy table");
+  int dev = 0, sms = 0, per_sm = 0;
+  if ((e = cudaGetDevice(&dev)) != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+  if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rs_copy_kernel, kBlock, 0)) != cudaSuccess)
+    return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+  per_sm = (int)std::min<uint64_t>((uint64_t)std::max(per_sm, 1), env_u64("SUIKA_RS_CTAS_PER_SM", 4));
+  const uint64_t grid = std::min<uint64_t>(ntiles, (uint64_t)sms * (uint64_t)per_sm);
+  rs_copy_kernel<<<(unsigned)grid, kBlock, 0, st>>>(reinterpret_cast<const DevSeg*>(workspace_dev), (int32_t)table.size(), ntiles);
+  if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(e, "rs_copy_launch: kernel launch");
+  if (info) {
+    info->n_tiles = ntiles;
+    info->total_bytes = total;
+    info->grid = (int32_t)grid;
+    info->block = kBlock;
+  }
+  return RS_OK;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------------------------
+// Peer memory: CUDA IPC export/import of the allocations that hold source tensors. A target
+// rank maps each peer allocation it reads once and pulls from it with rs_copy_launch.
+// ---------------------------------------------------------------------------------------------
+namespace {
+typedef CUresult (*GetAddressRangeFn)(CUdeviceptr*, size_t*, CUdeviceptr);
+
+int address_range(const void* ptr, uint64_t* base, uint64_t* bytes) {
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  cudaError_t e = cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn, cudaEnableDefault, &q);
+  if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn)
+    return efail(RS_ERR_PEER, "rs_peer_export: cuMemGetAddressRange entry point unavailable");
+  CUdeviceptr b = 0;
+  size_t n = 0;
+  const CUresult r = reinterpret_cast<GetAddressRangeFn>(fn)(&b, &n, reinterpret_cast<CUdeviceptr>(ptr));
+  if (r != CUDA_SUCCESS) return efail(RS_ERR_PEER, "rs_peer_export: cuMemGetAddressRange failed (" + std::to_string((int)r) + ")");
+  *base = (uint64_t)b;
+  *bytes = (uint64_t)n;
+  return RS_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int rs_peer_export(const void* ptr_dev, rs_peer_handle* out, uint64_t* offset) {
+  if (!ptr_dev || !out || !offset) return efail(RS_ERR_ARG, "rs_peer_export: NULL argument");
+  std::memset(out, 0, sizeof(*out));
+  cudaPointerAttributes attr;
+  cudaError_t e = cudaPointerGetAttributes(&attr, ptr_dev);
+  if (e != cudaSuccess) return cuda_fail(e, "rs_peer_export: cudaPointerGetAttributes");
+  if (attr.type != cudaMemoryTypeDevice) return efail(RS_ERR_PEER, "rs_peer_export: pointer is not device memory");
+  uint64_t base = 0, bytes = 0;
+  int rc = address_range(ptr_dev, &base, &bytes);
+  if (rc) return rc;
+  cudaIpcMemHandle_t h;
+  if ((e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base))) != cudaSuccess)
+    return cuda_fail(e, "rs_peer_export: cudaIpcGetMemHandle (the allocation must come from cudaMalloc; "
+                        "PyTorch's expandable segments are not exportable this way)");
+  static_assert(sizeof(h) <= sizeof(out->ipc), "IPC handle size");
+  std::memcpy(out->ipc, &h, sizeof(h));
+  out->alloc_base = base;
+  out->alloc_bytes = bytes;
+  out->device = attr.device;
+  out->pid = (int32_t)getpid();
+  *offset = (uint64_t)reinterpret_cast<uintptr_t>(ptr_dev) - base;
+  return RS_OK;
+}
+
+int rs_peer_open(const rs_peer_handle* handle, void** base_dev) {
+  if (!handle || !base_dev) return efail(RS_ERR_ARG, "rs_peer_open: NULL argument");
+  *base_dev = nullptr;
+  if (handle->pid == (int32_t)getpid())
+    return efail(RS_ERR_PEER, "rs_peer_open: handle exported by this process; use the local address");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle->ipc, sizeof(h));
+  void* p = nullptr;
+  cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_fail(e, "rs_peer_open: cudaIpcOpenMemHandle");
+  *base_dev = p;
+  return RS_OK;
+}
+
+int rs_peer_close(void* base_dev) {
+  if (!base_dev) return efail(RS_ERR_ARG, "rs_peer_close: NULL argument");
+  cudaError_t e = cudaIpcCloseMemHandle(base_dev);
+  if (e != cudaSuccess) return cuda_fail(e, "rs_peer_close: cudaIpcCloseMemHandle");
+  return RS_OK;
+}
+
+}  // extern "C"

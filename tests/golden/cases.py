@@ -1,0 +1,36 @@
+"""Parity cases shared by the golden generator and the tests.
+
+Full-width BASELINE shapes are too large for a CPU run of the reference, so most cases keep the
+reference's tensor names, module order and slicing at reduced widths and depths; cfg1 runs at its
+full size. Each case names the reshard (meshes) of the BASELINE configuration it stands for.
+"""
+from suika_b200.layouts import CONFIGS, SPECS, ReshardConfig, scaled_spec
+
+_llama_mini = scaled_spec(SPECS["llama2-13b"], name="llama-mini", hidden=256, n_layers=4, n_heads=8, ffn=512, vocab=512)
+_gpt_mini = scaled_spec(SPECS["gpt-6.7b"], name="gpt-mini", hidden=128, n_layers=4, n_heads=4, ffn=512, vocab=256, pos_emb=64)
+_qwen_mini = scaled_spec(SPECS["qwen2-7b"], name="qwen-mini", hidden=256, n_layers=4, n_heads=8, n_kv_heads=4, head_dim=32,
+                         ffn=512, vocab=512)
+_odd = scaled_spec(SPECS["llama-small"], name="llama-odd", hidden=24, n_layers=3, n_heads=2, ffn=40, vocab=50)
+
+
+def _cfg(name, spec, base=None, src=None, dst=None, note=""):
+    b = CONFIGS[base] if base else None
+    return ReshardConfig(name, spec, src if src is not None else b.src_mesh, dst if dst is not None else b.dst_mesh, note or (b.note if b else ""))
+
+
+CASES = {
+    "cfg1": {"config": CONFIGS["cfg1"], "description": "cfg1 at full size: small Llama TP1xPP2 -> TP2xPP1 (2 ranks)"},
+    "cfg2_mini": {"config": _cfg("cfg2_mini", _llama_mini, "cfg2"), "description": "Llama (reduced) TP2xPP2xDP2 -> TP4xPP1xDP2 (8 ranks)"},
+    "cfg2_mini_noib": {"config": _cfg("cfg2_mini_noib", _llama_mini, "cfg2"), "ib_disabled": True,
+                       "description": "as cfg2_mini with NCCL_IB_DISABLE=1 (minimum_est_peers = 2)"},
+    "cfg2b_mini": {"config": _cfg("cfg2b_mini", _llama_mini, "cfg2b"), "description": "Llama (reduced) TP1 -> TP2 (2 ranks)"},
+    "cfg3_mini": {"config": _cfg("cfg3_mini", _llama_mini, "cfg3"), "description": "Llama (reduced) TP8xPP1 -> TP4xPP2 (8 ranks), TP shrink"},
+    "cfg4_mini": {"config": _cfg("cfg4_mini", _gpt_mini, "cfg4"), "description": "GPT (reduced, wpe) TP2xPP2 on 4 -> TP2xPP2xDP2 on 8"},
+    "cfg5_mini": {"config": _cfg("cfg5_mini", _qwen_mini, "cfg5"), "description": "Qwen2 (reduced, GQA, QKV bias) TP4xPP2 -> TP2xPP2xDP2"},
+    "shrink_mini": {"config": _cfg("shrink_mini", _llama_mini, src=[[[0, 1, 2, 3]], [[4, 5, 6, 7]]], dst=[[[0, 1]]]),
+                    "description": "Llama (reduced) TP4xPP2 on 8 -> TP2 on 2 (shrink, runs in the old world)"},
+    "hetero_mini": {"config": _cfg("hetero_mini", _llama_mini, src=[[[0], [1, 2]]], dst=[[[0, 1, 2, 3]]]),
+                    "description": "Llama (reduced) DP groups of unequal TP (TP1 + TP2) -> TP4"},
+    "odd_mini": {"config": _cfg("odd_mini", _odd, src=[[[0]], [[1]]], dst=[[[0, 1]]]),
+                 "description": "odd widths (rows not 16-byte multiples) TP1xPP2 -> TP2"},
+}
