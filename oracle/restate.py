@@ -153,13 +153,27 @@ def execute_rank(ops: Sequence[Op], states, subfields: Sequence[Tuple[str, bool]
 
 
 def execute_world(ops, states, subfields, ranks: Sequence[int], order: str = "reference", threads: int = 1):
-    """execute_rank for every target rank; `threads` > 1 runs ranks on a thread pool (numpy copies
-    release the GIL)."""
+    """execute_rank for every target rank. With threads > 1 the work is split by (rank, tensor)
+    over a thread pool: every target tensor depends only on its own ops, and numpy's copies
+    release the GIL."""
     if threads <= 1:
         return {r: execute_rank(ops, states, subfields, r, order) for r in ranks}
+    tasks = []
+    for r in ranks:
+        names = list(dict.fromkeys(o.name for o in ops if o.dst == r))
+        for k in range(threads):
+            part = set(names[k::threads])
+            if part:
+                tasks.append((r, [o for o in ops if o.name in part and (o.dst == r or o.src == r)]))
     with ThreadPoolExecutor(max_workers=threads) as ex:
-        futs = {r: ex.submit(execute_rank, ops, states, subfields, r, order) for r in ranks}
-        return {r: f.result() for r, f in futs.items()}
+        futs = [(r, ex.submit(execute_rank, sub_ops, states, subfields, r, order)) for r, sub_ops in tasks]
+        out = {r: {} for r in ranks}
+        for r, f in futs:
+            out[r].update(f.result())
+    for r in ranks:  # restore the reference's tensor order
+        order_r = list(dict.fromkeys(o.name for o in ops if o.dst == r))
+        out[r] = {n: out[r][n] for n in order_r}
+    return out
 
 
 def semantic_target(states, spl, tpl, subfields, rank: int) -> Dict[str, Dict[str, np.ndarray]]:

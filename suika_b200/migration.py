@@ -333,9 +333,448 @@ def launch_copies(descs: np.ndarray, device: torch.device, stream: Optional[torc
     ws_bytes = C.c_uint64()
     L.check(lib.rs_copy_workspace_bytes(n, C.byref(ws_bytes)))
     ws = torch.empty(int(ws_bytes.value), dtype=torch.uint8, device=device)
+    current = torch.cuda.current_stream(device)
     if stream is None:
-        stream = torch.cuda.current_stream(device)
-    # The workspace is freed into the stream-ordered caching allocator after the launch, so it is
-    # reused only by work queued behind this kernel on the same stream.
+        stream = current
+    elif stream != current:
+        stream.wait_stream(current)  # sources, targets and staging were produced on the current stream
+        ws.record_stream(stream)
+    # The workspace goes back to the stream-ordered caching allocator after the launch, so it is
+    # reused only by work queued behind this kernel.
     L.check(lib.rs_copy_launch(descs.ctypes.data, n, ws.data_ptr(), ws.numel(), C.c_void_p(stream.cuda_stream), C.byref(info)))
     return info
+
+
+# ---------------------------------------------------------------------------------------------
+# Shared execution helpers.
+# ---------------------------------------------------------------------------------------------
+def _is_meta_field(field_type) -> bool:
+    """execute_param_transfer's is_meta_tensor (migration.py:423-424)."""
+    return not (isinstance(field_type, str) and field_type == "normal")
+
+
+class _NullProf:
+    def start(self, *a, **k):
+        pass
+
+    def stop(self, *a, **k):
+        pass
+
+
+def _sub_dtypes(expected_sub_fields, states: Iterable[Dict[str, Dict[str, torch.Tensor]]]) -> Dict[str, torch.dtype]:
+    """dtype of every normal sub-field, read from the first source entry that has it. The
+    reference allocates received pieces in the layout dtype (migration.py:285-287), which only
+    works when every sub-field has the param's dtype; here each sub-field keeps its own dtype."""
+    out: Dict[str, torch.dtype] = {}
+    want = [s for s, ft in expected_sub_fields if not _is_meta_field(ft)]
+    for st in states:
+        for ent in st.values():
+            for s in want:
+                if s not in out and s in ent:
+                    out[s] = ent[s].dtype
+            if len(out) == len(want):
+                return out
+    return out
+
+
+def _program_spec(expected_sub_fields, dtypes: Dict[str, torch.dtype]):
+    spec = []
+    for s, ft in expected_sub_fields:
+        if _is_meta_field(ft):
+            spec.append((ft.dtype.itemsize, True))
+        else:
+            if s not in dtypes:
+                raise AssertionError(f"expected_sub_fields mismatch: no source tensor carries sub-field {s}")
+            spec.append((dtypes[s].itemsize, False))
+    return spec
+
+
+def _name_order(plan: Plan, rank: int) -> List[int]:
+    """Target tensor order of a rank: first op per name (target_state_dict creation, migration.py:431-433)."""
+    ops = plan.op_array
+    ids = ops["name_id"][ops["dst_rank"] == rank]
+    if len(ids) == 0:
+        return []
+    _, first = np.unique(ids, return_index=True)
+    return [int(x) for x in ids[np.sort(first)]]
+
+
+def _check_source(t: torch.Tensor, name: str, sub: str, device: torch.device, dtype: torch.dtype) -> torch.Tensor:
+    if t.device != device:
+        raise RuntimeError(f"source {name}[{sub}] is on {t.device}, expected {device}")
+    if t.dtype.itemsize != dtype.itemsize:
+        raise AssertionError(f"source {name}[{sub}] has dtype {t.dtype}, sub-field dtype is {dtype}")
+    return t if t.is_contiguous() else t.contiguous()
+
+
+class _MetaStage:
+    """Singleton sub-fields: values gathered on the host, uploaded once, and written into their
+    own target tensors by 4-byte entries of the same copy table."""
+
+    def __init__(self, device: torch.device):
+        self.device = device
+        self.values: List[bytes] = []
+        self.targets: List[torch.Tensor] = []
+
+    def add(self, value: torch.Tensor, out: torch.Tensor) -> None:
+        v = value.detach().reshape(-1)
+        if v.numel() != 1 or v.element_size() != out.element_size():
+            raise AssertionError(f"singleton sub-field of {v.numel()} x {v.dtype} cannot fill {out.dtype}")
+        self.values.append(v.cpu().view(torch.uint8).numpy().tobytes())
+        self.targets.append(out)
+
+    def descs(self) -> Tuple[np.ndarray, Optional[torch.Tensor]]:
+        if not self.targets:
+            return np.zeros(0, dtype=L.COPY_DESC_DTYPE), None
+        sizes = [len(v) for v in self.values]
+        offs = np.cumsum([0] + [(s + 15) // 16 * 16 for s in sizes])
+        host = np.zeros(int(offs[-1]), dtype=np.uint8)
+        for o, v in zip(offs, self.values):
+            host[o:o + len(v)] = np.frombuffer(v, dtype=np.uint8)
+        stage = torch.from_numpy(host).to(self.device)
+        d = np.zeros(len(self.targets), dtype=L.COPY_DESC_DTYPE)
+        base = stage.data_ptr()
+        for i, (o, s, t) in enumerate(zip(offs, sizes, self.targets)):
+            d[i] = (base + int(o), t.data_ptr(), 1, s, s, s)
+        return d, stage
+
+
+def _meta_target(value: torch.Tensor, first_is_self: bool, field_type, device: torch.device) -> torch.Tensor:
+    """Shape/dtype the reference gives a singleton target: the source tensor's own when the first
+    piece is a self transfer (migration.py:446), [1] in the field's dtype when received (:486-487)."""
+    if first_is_self:
+        return torch.empty(value.shape, dtype=value.dtype, device=device)
+    return torch.empty((1,), dtype=field_type.dtype, device=device)
+
+
+# ---------------------------------------------------------------------------------------------
+# All ranks of a reshard on one device.
+# ---------------------------------------------------------------------------------------------
+def reshard_local(source_param_layout, target_param_layout, source_state_dicts: Dict[int, Dict[str, Dict[str, torch.Tensor]]],
+                  expected_sub_fields, device=None, views: bool = False, order: str = "reference",
+                  src_choice: str = "reference", minimum_est_peers: Optional[int] = None, plan: Optional[Plan] = None,
+                  stream: Optional[torch.cuda.Stream] = None, return_info: bool = False):
+    """Reshard every rank's state on one device: {src rank: state} -> {dst rank: state}.
+
+    The target of each rank equals what execute_param_transfer returns on that rank. With
+    views=True a target that is one contiguous range of one source tensor (a dim-0 TP slice or a
+    replicated tensor) is returned as a view of it instead of a copy, so only row-strided pieces
+    move (the "TP1 -> TP2 views" relayout); views=False copies everything like the reference.
+    Asynchronous on `stream`; synchronise before reading the targets.
+    """
+    device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    if device.type != "cuda":
+        raise RuntimeError("suika_b200.reshard_local runs on a CUDA device only")
+    plan = plan or Plan(source_param_layout, target_param_layout, order=order, src_choice=src_choice,
+                        minimum_est_peers=minimum_est_peers)
+    dtypes = _sub_dtypes(expected_sub_fields, source_state_dicts.values())
+    spec = _program_spec(expected_sub_fields, dtypes)
+    subs = [s for s, _ in expected_sub_fields]
+    meta = _MetaStage(device)
+    tables = []
+    out: Dict[int, Dict[str, Dict[str, torch.Tensor]]] = {}
+    for rank, metas in target_param_layout.layout.items():
+        if not metas:
+            continue
+        prog = plan.program(rank, spec)
+        srcs = []
+        for ss in prog.src_slots:
+            name, sub = plan.names[ss["name_id"]], subs[ss["subfield"]]
+            srcs.append(_check_source(source_state_dicts[int(ss["src_rank"])][name][sub], name, sub, device, dtypes[sub]))
+        seg_count = np.bincount(prog.segments["dst_slot"], minlength=len(prog.dst_slots)) if len(prog.segments) else np.zeros(len(prog.dst_slots), int)
+        first_seg = {}
+        for i, sg in enumerate(prog.segments):
+            first_seg.setdefault(int(sg["dst_slot"]), i)
+        dst_t, keep = [], np.ones(len(prog.segments), dtype=bool)
+        for k, ds in enumerate(prog.dst_slots):
+            sub = subs[ds["subfield"]]
+            shape = tuple(int(x) for x in ds["shape"][: ds["ndim"]])
+            t = None
+            if views and seg_count[k] == 1:
+                sg = prog.segments[first_seg[k]]
+                if sg["rows"] == 1 and sg["row_bytes"] == ds["nbytes"]:
+                    src = srcs[sg["src_slot"]]
+                    e0 = int(sg["src_offset"]) // src.element_size()
+                    t = src.reshape(-1)[e0:e0 + int(ds["nbytes"]) // src.element_size()].view(shape)
+                    keep[first_seg[k]] = False
+            if t is None:
+                t = torch.empty(shape, dtype=dtypes[sub], device=device)
+            dst_t.append(t)
+        if len(prog.segments):
+            d = prog.resolve(np.array([t.data_ptr() for t in srcs], np.uint64),
+                             np.array([t.numel() * t.element_size() for t in srcs], np.uint64),
+                             np.array([t.data_ptr() for t in dst_t], np.uint64),
+                             np.array([t.numel() * t.element_size() for t in dst_t], np.uint64))
+            tables.append(d[keep])
+        ent: Dict[str, Dict[str, torch.Tensor]] = {}
+        for ds, t in zip(prog.dst_slots, dst_t):
+            ent.setdefault(plan.names[ds["name_id"]], {})[subs[ds["subfield"]]] = t
+        for ms in prog.meta_slots:
+            name, sub = plan.names[ms["name_id"]], subs[ms["subfield"]]
+            v = source_state_dicts[int(ms["src_rank"])][name][sub]
+            t = _meta_target(v, bool(ms["first_is_self"]), expected_sub_fields[ms["subfield"]][1], device)
+            meta.add(v, t)
+            ent.setdefault(name, {})[sub] = t
+        out[rank] = {plan.names[n]: {s: ent[plan.names[n]][s] for s in subs if s in ent[plan.names[n]]}
+                     for n in _name_order(plan, rank)}
+    md, stage = meta.descs()
+    table = np.concatenate(tables + [md]) if (tables or len(md)) else np.zeros(0, dtype=L.COPY_DESC_DTYPE)
+    info = launch_copies(table, device, stream)
+    if stage is not None and stream is not None:
+        stage.record_stream(stream)
+    if return_info:
+        return out, info, table
+    return out
+
+
+# ---------------------------------------------------------------------------------------------
+# One rank per process: the drop-in for schedule_and_execute_param_transfer.
+# ---------------------------------------------------------------------------------------------
+class _PeerMaps:
+    """Peer allocations mapped into this process for one call; closed together at the end."""
+
+    def __init__(self):
+        self._lib = L.load()
+        self.bases: Dict[Tuple[int, int], int] = {}
+
+    def base(self, peer: int, alloc: int, handle_bytes: bytes) -> int:
+        key = (peer, alloc)
+        if key not in self.bases:
+            h = L.RsPeerHandle.from_buffer_copy(handle_bytes)
+            p = C.c_void_p()
+            L.check(self._lib.rs_peer_open(C.byref(h), C.byref(p)))
+            self.bases[key] = int(p.value)
+        return self.bases[key]
+
+    def close(self) -> None:
+        err = None
+        for p in self.bases.values():
+            rc = self._lib.rs_peer_close(C.c_void_p(p))
+            if rc != L.RS_OK and err is None:
+                err = rc
+        self.bases.clear()
+        if err is not None:
+            L.check(err)
+
+
+def _export(tensors: List[torch.Tensor]):
+    """Export the allocations holding `tensors`: ([handle bytes per allocation], [(alloc, offset)])."""
+    lib = L.load()
+    handles: List[bytes] = []
+    index: Dict[int, int] = {}
+    where = []
+    for t in tensors:
+        h = L.RsPeerHandle()
+        off = C.c_uint64()
+        L.check(lib.rs_peer_export(C.c_void_p(t.data_ptr()), C.byref(h), C.byref(off)))
+        if h.alloc_base not in index:
+            index[h.alloc_base] = len(handles)
+            handles.append(bytes(h))
+        where.append((index[h.alloc_base], int(off.value)))
+    return handles, where
+
+
+class RankTransfer:
+    """One rank's share of a reshard, split into prepare / launch / finish so that the data path
+    (launch) can be run and timed on its own.
+
+    prepare (constructor, collective over `world`): export the allocations of the source tensors
+    other ranks read from this rank; exchange handles, offsets, sub-field dtypes and singleton
+    values in one all_gather_object; map the peer allocations this rank reads (CUDA IPC); allocate
+    the targets; bind the copy program to addresses (bounds-checked).
+    launch: one kernel launch pulls every piece (peer HBM over NVLink, own HBM locally).
+    finish (collective): a barrier after this rank's kernel has finished keeps every source alive
+    until its last reader is done; then peer mappings are closed and source_state_dict is cleared
+    (migration.py:527).
+    """
+
+    def __init__(self, plan: Plan, source_state_dict: Dict[str, Dict[str, torch.Tensor]], expected_sub_fields,
+                 device: torch.device, world: Optional[dist.ProcessGroup] = None, log_func: Optional[Callable] = None):
+        self.plan, self.device, self.world = plan, device, world
+        self.source_state_dict = source_state_dict
+        self.log = log_func or (lambda m: None)
+        self.rank = rank = dist.get_rank(world)
+        ws = dist.get_world_size(world)
+        subs = [s for s, _ in expected_sub_fields]
+        sidx = {s: i for i, s in enumerate(subs)}
+        ops = plan.op_array
+        # 1. what peers read from this rank
+        mask = (ops["src_rank"] == rank) & (ops["dst_rank"] != rank)
+        served = [int(x) for x in np.unique(ops["name_id"][mask])]
+        exp_tensors, exp_keys, meta_vals = [], [], {}
+        for nid in served:
+            name = plan.names[nid]
+            if name not in source_state_dict:
+                raise AssertionError(f"[{rank}]: param missing in source {name}")
+            ent = source_state_dict[name]
+            for s, ft in expected_sub_fields:
+                if s not in ent:
+                    raise AssertionError(f"expected_sub_fields mismatch: {name} has no {s}")
+                v = ent[s]
+                if _is_meta_field(ft):
+                    meta_vals[(nid, sidx[s])] = (v.detach().reshape(-1).cpu().view(torch.uint8).numpy().tobytes(), str(v.dtype), tuple(v.shape))
+                else:
+                    if v.device != device:
+                        raise RuntimeError(f"source {name}[{s}] is on {v.device}, expected {device}")
+                    if not v.is_contiguous():
+                        v = ent[s] = v.contiguous()
+                    exp_tensors.append(v)
+                    exp_keys.append((nid, sidx[s], v.numel() * v.element_size()))
+        handles, where = _export(exp_tensors)
+        my_dtypes = {s: str(d).replace("torch.", "") for s, d in _sub_dtypes(expected_sub_fields, [source_state_dict]).items()}
+        torch.cuda.current_stream(device).synchronize()  # sources are complete before any peer reads them
+        info = {"handles": handles, "tensors": {k[:2]: (a, o, k[2]) for k, (a, o) in zip(exp_keys, where)},
+                "meta": meta_vals, "dtypes": my_dtypes}
+        gathered: List[Any] = [None] * ws
+        dist.all_gather_object(gathered, info, group=world)
+        # 2. this rank's program, bound to local, peer and freshly allocated target addresses
+        dtypes: Dict[str, torch.dtype] = {}
+        for g in gathered:
+            for s, d in g["dtypes"].items():
+                dtypes.setdefault(s, getattr(torch, d))
+        self.target: Dict[str, Dict[str, torch.Tensor]] = {}
+        self.table = np.zeros(0, dtype=L.COPY_DESC_DTYPE)
+        self.remote_bytes = self.local_bytes = 0
+        self._stage = None
+        self.peers = _PeerMaps()
+        if not np.any(ops["dst_rank"] == rank):
+            return
+        try:
+            spec = _program_spec(expected_sub_fields, dtypes)
+            prog = plan.program(rank, spec)
+            src_ptr = np.zeros(len(prog.src_slots), np.uint64)
+            src_ext = np.zeros(len(prog.src_slots), np.uint64)
+            for i, ss in enumerate(prog.src_slots):
+                nid, sf, sr = int(ss["name_id"]), int(ss["subfield"]), int(ss["src_rank"])
+                if sr == rank:
+                    name = plan.names[nid]
+                    if name not in source_state_dict:
+                        raise AssertionError(f"[{rank}]: param missing in source {name}")
+                    v = _check_source(source_state_dict[name][subs[sf]], name, subs[sf], device, dtypes[subs[sf]])
+                    source_state_dict[name][subs[sf]] = v
+                    src_ptr[i], src_ext[i] = v.data_ptr(), v.numel() * v.element_size()
+                else:
+                    a, o, nb = gathered[sr]["tensors"][(nid, sf)]
+                    src_ptr[i] = self.peers.base(sr, a, gathered[sr]["handles"][a]) + o
+                    src_ext[i] = nb
+            dst_t = []
+            for ds in prog.dst_slots:
+                shape = tuple(int(x) for x in ds["shape"][: ds["ndim"]])
+                dst_t.append(torch.empty(shape, dtype=dtypes[subs[ds["subfield"]]], device=device))
+            table = prog.resolve(src_ptr, src_ext, np.array([x.data_ptr() for x in dst_t], np.uint64),
+                                 np.array([x.numel() * x.element_size() for x in dst_t], np.uint64))
+            ent: Dict[str, Dict[str, torch.Tensor]] = {}
+            for ds, x in zip(prog.dst_slots, dst_t):
+                ent.setdefault(plan.names[ds["name_id"]], {})[subs[ds["subfield"]]] = x
+            meta = _MetaStage(device)
+            for ms in prog.meta_slots:
+                nid, sf, sr = int(ms["name_id"]), int(ms["subfield"]), int(ms["src_rank"])
+                name, s = plan.names[nid], subs[sf]
+                if sr == rank:
+                    v = source_state_dict[name][s]
+                else:
+                    raw, dt, shape = gathered[sr]["meta"][(nid, sf)]
+                    v = torch.frombuffer(bytearray(raw), dtype=torch.uint8).view(getattr(torch, dt.replace("torch.", ""))).reshape(shape)
+                x = _meta_target(v, bool(ms["first_is_self"]), expected_sub_fields[sf][1], device)
+                meta.add(v, x)
+                ent.setdefault(name, {})[s] = x
+            md, self._stage = meta.descs()
+            self.table = np.concatenate([table, md])
+            self.remote_bytes, self.local_bytes = prog.remote_bytes, prog.local_bytes
+            self.target = {plan.names[n]: {s: ent[plan.names[n]][s] for s in subs if s in ent[plan.names[n]]}
+                           for n in _name_order(plan, rank)}
+        except BaseException:
+            self.peers.close()
+            raise
+
+    def launch(self, stream: Optional[torch.cuda.Stream] = None) -> L.RsLaunchInfo:
+        """Queue this rank's pulls (asynchronous; one kernel launch)."""
+        return launch_copies(self.table, self.device, stream)
+
+    def finish(self) -> Dict[str, Dict[str, torch.Tensor]]:
+        """Wait for this rank's kernel, then for every rank (barrier); release peers and sources."""
+        try:
+            torch.cuda.current_stream(self.device).synchronize()
+            dist.barrier(group=self.world)  # every reader of this rank's sources has finished
+        finally:
+            self.peers.close()
+        self._stage = None
+        self.source_state_dict.clear()
+        self.log(f"suika_b200: rank {self.rank} pulled {self.remote_bytes} B from peers and {self.local_bytes} B "
+                 f"locally with {len(self.table)} copies")
+        return self.target
+
+
+def execute_plan_distributed(plan: Plan, source_state_dict: Dict[str, Dict[str, torch.Tensor]], expected_sub_fields,
+                             device: torch.device, world: Optional[dist.ProcessGroup] = None,
+                             log_func: Optional[Callable] = None, timers: Optional[dict] = None):
+    """Run one rank's share of a reshard (execute_param_transfer, migration.py:397-556): prepare,
+    one kernel launch, finish (see RankTransfer). Collective over `world`."""
+    rt = RankTransfer(plan, source_state_dict, expected_sub_fields, device, world, log_func)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    info = rt.launch()
+    ev1.record()
+    target = rt.finish()
+    if timers is not None:
+        timers["kernel_ms"] = ev0.elapsed_time(ev1)
+        timers["n_tiles"], timers["total_bytes"] = int(info.n_tiles), int(info.total_bytes)
+        timers["remote_bytes"], timers["local_bytes"] = rt.remote_bytes, rt.local_bytes
+    return target
+
+
+def schedule_and_execute_param_transfer(source_param_layout, target_param_layout, source_state_dict: Dict[str, Dict[str, torch.Tensor]],
+                                        other_context_dict: Dict[str, Any], device, world: Optional[dist.ProcessGroup],
+                                        prof=None, forcefully_free: bool = False, log_func=None):
+    """Drop-in for Suika's schedule_and_execute_param_transfer (migration.py:558-598).
+
+    Same arguments, same return value ({name: {sub_field: tensor}} of this rank, tensors new and
+    contiguous), same side effect (source_state_dict cleared). The targets are byte-identical to
+    the reference's, including its order of concatenated pieces. `forcefully_free` is accepted for
+    signature compatibility: no temporary piece tensors exist to free.
+    """
+    if not isinstance(device, torch.device):
+        device = torch.device(device)
+    if device.type != "cuda":
+        raise RuntimeError("suika_b200 moves state on CUDA devices only (no CPU path)")
+    prof = prof or _NullProf()
+    prof.start("schedule")
+    plan = Plan(source_param_layout, target_param_layout)
+    prof.stop("schedule")
+    prof.start("execute", require_memory=True)
+    target = execute_plan_distributed(plan, source_state_dict, other_context_dict["expected_sub_fields"], device, world, log_func)
+    torch.cuda.synchronize(device=device)
+    prof.stop("execute", require_memory=True)
+    return target
+
+
+class TransferSchedule(list):
+    """The list of TransferOps schedule_param_transfer returns, carrying the C plan that
+    execute_param_transfer runs."""
+
+    def __init__(self, plan: Plan):
+        super().__init__(plan.transfer_ops())
+        self.plan = plan
+
+
+def schedule_param_transfer(source_param_layout, target_param_layout, log_func: Optional[Callable] = None) -> TransferSchedule:
+    """Drop-in for schedule_param_transfer (migration.py:322-381)."""
+    plan = Plan(source_param_layout, target_param_layout)
+    if log_func is not None:
+        for o in plan.op_array[plan.op_array["src_rank"] != plan.op_array["dst_rank"]]:
+            log_func(f"schedule_param_transfer: {int(o['src_rank'])} > {int(o['dst_rank'])} transfer {plan.names[o['name_id']]}")
+    return TransferSchedule(plan)
+
+
+def execute_param_transfer(transfer_ops: TransferSchedule, source_state_dict, device, expected_sub_fields, world=None,
+                           log_func=None, prof=None, forcefully_free: bool = False, fake_source_state_dicts=None):
+    """Drop-in for execute_param_transfer (migration.py:397-556) on a schedule made by
+    schedule_param_transfer above (the C plan travels with it)."""
+    if not isinstance(transfer_ops, TransferSchedule):
+        raise TypeError("execute_param_transfer needs the schedule returned by suika_b200's schedule_param_transfer")
+    if fake_source_state_dicts is not None:
+        raise NotImplementedError("the checkpoint-resume path (fake_source_state_dicts) is not built yet")
+    device = torch.device(device)
+    if device.type != "cuda":
+        raise RuntimeError("suika_b200 moves state on CUDA devices only (no CPU path)")
+    return execute_plan_distributed(transfer_ops.plan, source_state_dict, expected_sub_fields, device, world, log_func)

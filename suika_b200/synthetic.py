@@ -85,11 +85,14 @@ def host_shard(full: np.ndarray, tp_meta) -> np.ndarray:
     return np.ascontiguousarray(np.split(full, g, axis=d)[i])
 
 
-def host_states(layout, subfields=SUBFIELDS, seed: int = 0, distinct_steps: bool = False) -> Dict[int, Dict[str, Dict[str, np.ndarray]]]:
-    """rank -> name -> sub-field -> host array for every tensor of a ParamLayout."""
+def host_states(layout, subfields=SUBFIELDS, seed: int = 0, distinct_steps: bool = False,
+                ranks: Optional[Sequence[int]] = None) -> Dict[int, Dict[str, Dict[str, np.ndarray]]]:
+    """rank -> name -> sub-field -> host array for every tensor of a ParamLayout (only `ranks` if given)."""
     cache: Dict[Tuple[str, str], np.ndarray] = {}
     out: Dict[int, Dict[str, Dict[str, np.ndarray]]] = {}
     for rank, metas in layout.layout.items():
+        if ranks is not None and rank not in ranks:
+            continue
         rs = {}
         for name, m in metas.items():
             ent = {}

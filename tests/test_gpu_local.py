@@ -1,0 +1,126 @@
+"""GPU parity of the copy kernel: every golden case resharded on one B200 (all ranks emulated on
+one device through reshard_local) must reproduce the reference's bytes, and the oracle's."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import restate as O
+from suika_b200 import migration as M
+from suika_b200 import synthetic as S
+from tests.golden.cases import CASES
+from tests.helpers import SUB_META, SUBS, digest, golden_states, load_golden
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda", 0)
+
+
+def to_device(states):
+    kinds = dict(SUBS)
+    return {r: {n: {s: S.to_torch(a, kinds[s], DEV if kinds[s] != "meta" else None) for s, a in ent.items()}
+                for n, ent in st.items()} for r, st in states.items()}
+
+
+def host(t: torch.Tensor) -> np.ndarray:
+    t = t.detach().cpu().contiguous()
+    if t.dtype == torch.bfloat16:
+        t = t.view(torch.uint16)
+    return t.numpy()
+
+
+@pytest.mark.parametrize("case", sorted(CASES))
+def test_reshard_local_matches_reference_digests(case):
+    g = load_golden(case)
+    cfg = CASES[case]["config"]
+    spl, tpl = cfg.layouts()
+    states = golden_states(cfg, seed=g["seed"])
+    plan = M.Plan(spl, tpl, minimum_est_peers=g["minimum_est_peers"])
+    out = M.reshard_local(spl, tpl, to_device(states), S.expected_sub_fields(), DEV, plan=plan)
+    torch.cuda.synchronize()
+    for rank_s, want in g["ranks"].items():
+        got = out[int(rank_s)]
+        assert list(got) == want["order"]
+        for name, fields in want["digests"].items():
+            assert list(got[name]) == list(fields)
+            for sub, (shape, dtype, sha) in fields.items():
+                t = got[name][sub]
+                assert list(t.shape) == shape and str(t.dtype).replace("torch.", "") == dtype, (rank_s, name, sub)
+                assert t.device == DEV and t.is_contiguous()
+                assert digest(host(t)) == sha, (rank_s, name, sub)
+
+
+@pytest.mark.parametrize("case", ["cfg3_mini", "cfg5_mini", "odd_mini", "hetero_mini"])
+def test_reshard_local_semantic_order_matches_oracle(case):
+    cfg = CASES[case]["config"]
+    spl, tpl = cfg.layouts()
+    states = golden_states(cfg)
+    out = M.reshard_local(spl, tpl, to_device(states), S.expected_sub_fields(), DEV, order="semantic", minimum_est_peers=1)
+    torch.cuda.synchronize()
+    ops = O.schedule(spl, tpl, minimum_est_peers=1)
+    for rank, metas in tpl.layout.items():
+        if not metas:
+            continue
+        want = O.execute_rank(ops, states, SUB_META, rank, order="semantic")
+        for name, ent in want.items():
+            for sub, a in ent.items():
+                assert np.array_equal(host(out[rank][name][sub]).reshape(-1).view(np.uint8), a.reshape(-1).view(np.uint8)), (rank, name, sub)
+
+
+def test_views_move_only_row_split_pieces():
+    cfg = CASES["cfg2b_mini"]["config"]
+    spl, tpl = cfg.layouts()
+    states = golden_states(cfg)
+    dev_states = to_device(states)
+    out, info, table = M.reshard_local(spl, tpl, dev_states, S.expected_sub_fields(), DEV, views=True, return_info=True)
+    torch.cuda.synchronize()
+    ops = O.schedule(spl, tpl, minimum_est_peers=1)
+    moved = 0
+    for rank in (0, 1):
+        want = O.execute_rank(ops, states, SUB_META, rank)
+        for name, ent in want.items():
+            for sub, a in ent.items():
+                t = out[rank][name][sub]
+                assert np.array_equal(host(t).reshape(-1).view(np.uint8), a.reshape(-1).view(np.uint8))
+                if sub != "step":
+                    shares = t.untyped_storage().data_ptr() == dev_states[0][name][sub].untyped_storage().data_ptr()
+                    row_split = spl.layout[0][name].tp_meta is not None and spl.layout[0][name].tp_meta[0] == -1
+                    assert shares != row_split, (name, sub)
+                    moved += 0 if shares else t.numel() * t.element_size()
+    assert info.total_bytes == moved + 4 * len([1 for r in (0, 1) for _ in out[r]])  # + one 4-byte step per tensor
+
+
+@pytest.mark.parametrize("tile", ["256", "4096", "131072"])
+def test_copy_kernel_random_rectangles(tile, monkeypatch):
+    """Strided copies with random alignment, pitch and size (every vector width, column-split rows)
+    against torch's own copy of the same rectangles."""
+    monkeypatch.setenv("SUIKA_RS_TILE_BYTES", tile)
+    rng = np.random.default_rng(int(tile))
+    src = torch.randint(0, 255, (8 << 20,), dtype=torch.uint8, device=DEV)
+    dst = torch.zeros(16 << 20, dtype=torch.uint8, device=DEV)
+    want = torch.zeros_like(dst)
+    descs, dpos = [], 0
+    for _ in range(300):
+        rows = int(rng.integers(1, 40))
+        rb = int(rng.choice([1, 2, 3, 4, 6, 8, 16, 48, 100, 1024, 5000, 20000]))
+        sp = rb + int(rng.integers(0, 64))
+        dp = rb + int(rng.integers(0, 64))
+        so = int(rng.integers(0, src.numel() - rows * sp - 1))
+        if rng.random() < 0.5:
+            so -= so % 16
+        dpos += int(rng.integers(0, 17))
+        if dpos + rows * dp >= dst.numel():
+            break
+        descs.append((src.data_ptr() + so, dst.data_ptr() + dpos, rows, rb, sp, dp))
+        for r in range(rows):
+            want[dpos + r * dp: dpos + r * dp + rb] = src[so + r * sp: so + r * sp + rb]
+        dpos += rows * dp
+    table = np.array(descs, dtype=M.L.COPY_DESC_DTYPE)
+    M.launch_copies(table, DEV)
+    torch.cuda.synchronize()
+    assert torch.equal(dst, want)
+
+
+def test_empty_table_is_a_noop():
+    info = M.launch_copies(np.zeros(0, dtype=M.L.COPY_DESC_DTYPE), DEV)
+    assert info.n_tiles == 0
