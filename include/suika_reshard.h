@@ -114,6 +114,38 @@ int rs_plan_num_ops(const rs_plan* plan, int64_t* n_ops);
 int rs_plan_get_ops(const rs_plan* plan, rs_op* ops, int64_t capacity);
 void rs_plan_free(rs_plan* plan);
 
+/* ---- layouts the reference does not have ---------------------------------------------------
+ * A slice rule describes how a TP shard of one tensor is cut when it is not the reference's
+ * contiguous chunk. The slice dim is split into groups (e.g. Q, K, V of a fused QKV weight);
+ * group g covers [offset, offset + size) of the full slice dim and consists of `units` equal
+ * units (heads). Shard i of degree T holds, group after group, units [i*u/T, (i+1)*u/T) of each
+ * group when u >= T, or the single unit floor(i*u/T) when u < T (that unit is then replicated
+ * on T/u shards: GQA KV heads at TP above the KV head count). A tensor without a rule is cut into
+ * contiguous chunks, as the reference cuts it (Suika/tensor_parallel.py:200-204,378-381).
+ *
+ * rs_plan_build_rules plans by intersecting the slice intervals of every target shard with those
+ * of the source shards (works for any mix of rules and chunks, TP grow and shrink, replicas),
+ * writes pieces in slice order, and picks among replicas with the balanced rule. Its targets equal
+ * gathering each full tensor from the sources and re-slicing it by the target's rule. */
+#define RS_MAX_GROUPS 4
+
+typedef struct rs_slice_group {
+  int64_t offset;   /* first index of the group along the slice dim */
+  int64_t size;     /* extent of the group along the slice dim     */
+  int64_t units;    /* indivisible units (heads) in the group      */
+} rs_slice_group;
+
+typedef struct rs_slice_rule {
+  int32_t name_id;
+  int32_t n_groups;
+  rs_slice_group groups[RS_MAX_GROUPS];
+} rs_slice_rule;
+
+int rs_plan_build_rules(const rs_rank_layout* src, int32_t n_src,
+                        const rs_rank_layout* dst, int32_t n_dst,
+                        const rs_slice_rule* rules, int32_t n_rules,
+                        const rs_plan_opts* opts, rs_plan** out);
+
 /* ---- per-rank program: the op loop + post-process of execute_param_transfer --------------
  * (migration.py:426-545). For one executing rank it lists the tensors the rank must produce
  * (dst slots), the source tensors it reads (src slots, local or on a peer), the meta
@@ -206,23 +238,39 @@ int rs_program_resolve(const rs_program* prog,
                        const uint64_t* dst_dev, const uint64_t* dst_extent,
                        rs_copy_desc* out, int64_t capacity);
 
+/* Like rs_program_resolve, but only for the segments whose source slot lives on `src_rank`
+ * (the pieces that rank sends when targets are written by their sources); slots of other ranks
+ * may be 0. Writes *n_out entries. */
+int rs_program_resolve_from(const rs_program* prog, int32_t src_rank,
+                            const uint64_t* src_dev, const uint64_t* src_extent,
+                            const uint64_t* dst_dev, const uint64_t* dst_extent,
+                            rs_copy_desc* out, int64_t capacity, int64_t* n_out);
+
 /* ---- device execution (sm_100a) ----------------------------------------------------------
  * One launch executes a whole copy table: local HBM copies and pulls from peer HBM over
  * NVLink alike (a peer address comes from rs_peer_open). Replaces the per-tensor
  * isend/irecv + contiguous/cat/clone of migration.py:466,489,501,536-538. */
 
 typedef struct rs_launch_info {
-  uint64_t n_tiles;        /* work units the table was cut into */
-  uint64_t total_bytes;    /* bytes copied                      */
-  int32_t grid;            /* CTAs launched                     */
-  int32_t block;           /* threads per CTA                   */
+  uint64_t n_tiles;        /* work units the table was cut into        */
+  uint64_t total_bytes;    /* bytes copied                             */
+  int64_t n_entries;       /* non-empty entries staged                 */
+  int32_t grid;            /* CTAs launched                            */
+  int32_t block;           /* threads per CTA                          */
+  int32_t variant;         /* launch shape (SUIKA_RS_VARIANT, 1-based) */
+  int32_t reserved;
 } rs_launch_info;
 
-/* Device workspace the caller must provide to rs_copy_launch for n descriptors. */
+/* Device workspace the caller must provide to rs_copy_stage / rs_copy_launch for n descriptors. */
 int rs_copy_workspace_bytes(int64_t n_desc, uint64_t* bytes);
-/* Stage the table into workspace_dev (stream-ordered) and launch the copy kernel on stream
- * (a cudaStream_t; NULL = legacy default stream). Asynchronous: synchronise the stream
- * before reading the targets. n_desc == 0 is a no-op. */
+/* Cut the table into tiles and stage it into workspace_dev (stream-ordered copy on `stream`, a
+ * cudaStream_t; NULL = legacy default stream). Fills *info for rs_copy_run. */
+int rs_copy_stage(const rs_copy_desc* descs, int64_t n_desc, void* workspace_dev, uint64_t workspace_bytes,
+                  void* stream, rs_launch_info* info);
+/* Launch the copy kernel over a staged table (asynchronous; may be repeated while the workspace
+ * and every address in the table stay valid). Synchronise the stream before reading targets. */
+int rs_copy_run(const void* workspace_dev, const rs_launch_info* info, void* stream);
+/* rs_copy_stage + rs_copy_run. n_desc == 0 is a no-op. */
 int rs_copy_launch(const rs_copy_desc* descs, int64_t n_desc,
                    void* workspace_dev, uint64_t workspace_bytes,
                    void* stream, rs_launch_info* info);

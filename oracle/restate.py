@@ -176,25 +176,57 @@ def execute_world(ops, states, subfields, ranks: Sequence[int], order: str = "re
     return out
 
 
+def _spans(full_shape, tp, rule):
+    """Slice-dim intervals of a shard: the reference's chunk, or per group of a slice rule the
+    units [i*u/T, (i+1)*u/T) (u >= T) or the unit floor(i*u/T) (u < T, replicated)."""
+    d, i, g = tp
+    F = int(full_shape[d])
+    if not rule:
+        return [(i * F // g, (i + 1) * F // g)]
+    out = []
+    for off, size, units in rule:
+        usz = size // units
+        lo = i * (units // g) if units >= g else (i * units // g)
+        n = units // g if units >= g else 1
+        out.append((off + lo * usz, off + (lo + n) * usz))
+    return out
+
+
 def semantic_target(states, spl, tpl, subfields, rank: int) -> Dict[str, Dict[str, np.ndarray]]:
-    """Gather each full tensor from the source shards and re-slice it by the target rule."""
+    """Gather each full tensor from the source shards and re-slice it by the target rule (chunks,
+    or a `tp_rule` attribute on the metas)."""
     out = {}
     for name, m in tpl.layout[rank].items():
         out[name] = {}
+        owners = [(r, metas[name]) for r, metas in spl.layout.items() if name in metas]
         for s, meta in subfields:
-            owners = [(r, metas[name]) for r, metas in spl.layout.items() if name in metas]
             if meta:
                 out[name][s] = np.array(states[owners[0][0]][name][s], copy=True)
                 continue
-            tp0 = owners[0][1].tp_meta
-            if tp0 is None:
+            tps = [mm.tp_meta for _, mm in owners if mm.tp_meta is not None]
+            if not tps:
                 full = states[owners[0][0]][name][s]
             else:
-                deg = tp0[2]
-                by_idx = {}
+                d = tps[0][0]
+                a0 = states[owners[0][0]][name][s]
+                shape = list(int(x) for x in m.shape)
+                full = np.zeros(shape, dtype=a0.dtype)
                 for r, mm in owners:
-                    if mm.tp_meta[2] == deg:
-                        by_idx.setdefault(mm.tp_meta[1], states[r][name][s])
-                full = np.concatenate([by_idx[i] for i in range(deg)], axis=tp0[0])
-            out[name][s] = full if m.tp_meta is None else np.ascontiguousarray(np.split(full, m.tp_meta[2], axis=m.tp_meta[0])[m.tp_meta[1]])
+                    a = states[r][name][s]
+                    if mm.tp_meta is None:
+                        full = a.copy()
+                        break
+                    at = 0
+                    for lo, hi in _spans(shape, mm.tp_meta, getattr(mm, "tp_rule", None)):
+                        idx = [slice(None)] * len(shape)
+                        sidx = [slice(None)] * len(shape)
+                        idx[d], sidx[d] = slice(lo, hi), slice(at, at + hi - lo)
+                        full[tuple(idx)] = a[tuple(sidx)]
+                        at += hi - lo
+            if m.tp_meta is None:
+                out[name][s] = np.array(full, copy=True)
+            else:
+                d = m.tp_meta[0]
+                parts = [np.take(full, np.arange(lo, hi), axis=d) for lo, hi in _spans(m.shape, m.tp_meta, getattr(m, "tp_rule", None))]
+                out[name][s] = np.ascontiguousarray(np.concatenate(parts, axis=d))
     return out

@@ -54,6 +54,17 @@ class RsOp(C.Structure):
                 ("reserved", C.c_int32), ("numel", C.c_int64)]
 
 
+RS_MAX_GROUPS = 4
+
+
+class RsSliceGroup(C.Structure):
+    _fields_ = [("offset", C.c_int64), ("size", C.c_int64), ("units", C.c_int64)]
+
+
+class RsSliceRule(C.Structure):
+    _fields_ = [("name_id", C.c_int32), ("n_groups", C.c_int32), ("groups", RsSliceGroup * RS_MAX_GROUPS)]
+
+
 class RsSubfield(C.Structure):
     _fields_ = [("itemsize", C.c_int32), ("is_meta", C.c_int32)]
 
@@ -88,7 +99,8 @@ class RsCopyDesc(C.Structure):
 
 
 class RsLaunchInfo(C.Structure):
-    _fields_ = [("n_tiles", C.c_uint64), ("total_bytes", C.c_uint64), ("grid", C.c_int32), ("block", C.c_int32)]
+    _fields_ = [("n_tiles", C.c_uint64), ("total_bytes", C.c_uint64), ("n_entries", C.c_int64), ("grid", C.c_int32),
+                ("block", C.c_int32), ("variant", C.c_int32), ("reserved", C.c_int32)]
 
 
 class RsPeerHandle(C.Structure):
@@ -114,6 +126,8 @@ SIGNATURES = {
     "rs_version": (C.c_int, [C.POINTER(C.c_int32), C.POINTER(C.c_int32)]),
     "rs_plan_build": (C.c_int, [C.POINTER(RsRankLayout), C.c_int32, C.POINTER(RsRankLayout), C.c_int32,
                                 C.POINTER(RsPlanOpts), C.POINTER(_P)]),
+    "rs_plan_build_rules": (C.c_int, [C.POINTER(RsRankLayout), C.c_int32, C.POINTER(RsRankLayout), C.c_int32,
+                                      C.POINTER(RsSliceRule), C.c_int32, C.POINTER(RsPlanOpts), C.POINTER(_P)]),
     "rs_plan_num_ops": (C.c_int, [_P, C.POINTER(C.c_int64)]),
     "rs_plan_get_ops": (C.c_int, [_P, C.POINTER(RsOp), C.c_int64]),
     "rs_plan_free": (None, [_P]),
@@ -125,7 +139,10 @@ SIGNATURES = {
     "rs_program_segments": (C.c_int, [_P, _P, C.c_int64]),
     "rs_program_free": (None, [_P]),
     "rs_program_resolve": (C.c_int, [_P, _P, _P, _P, _P, _P, C.c_int64]),
+    "rs_program_resolve_from": (C.c_int, [_P, C.c_int32, _P, _P, _P, _P, _P, C.c_int64, C.POINTER(C.c_int64)]),
     "rs_copy_workspace_bytes": (C.c_int, [C.c_int64, C.POINTER(C.c_uint64)]),
+    "rs_copy_stage": (C.c_int, [_P, C.c_int64, _P, C.c_uint64, _P, C.POINTER(RsLaunchInfo)]),
+    "rs_copy_run": (C.c_int, [_P, C.POINTER(RsLaunchInfo), _P]),
     "rs_copy_launch": (C.c_int, [_P, C.c_int64, _P, C.c_uint64, _P, C.POINTER(RsLaunchInfo)]),
     "rs_peer_export": (C.c_int, [_P, C.POINTER(RsPeerHandle), C.POINTER(C.c_uint64)]),
     "rs_peer_open": (C.c_int, [C.POINTER(RsPeerHandle), C.POINTER(_P)]),

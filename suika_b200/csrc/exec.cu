@@ -50,7 +50,6 @@ struct DevSeg {
 };
 static_assert(sizeof(DevSeg) == 72, "DevSeg layout");
 
-constexpr int kBlock = 512;
 constexpr uint64_t kDefaultTileBytes = 128 * 1024;
 
 template <int VB> struct Vec;
@@ -91,7 +90,9 @@ __device__ __forceinline__ void store_vec(uint32_t* p, const uint32_t& v) { *p =
 __device__ __forceinline__ void store_vec(uint16_t* p, const uint16_t& v) { *p = v; }
 __device__ __forceinline__ void store_vec(uint8_t* p, const uint8_t& v) { *p = v; }
 
-// Copy an nr x (vpr * VB bytes) rectangle. U loads are issued before their stores.
+// Copy an nr x (vpr * VB bytes) rectangle. U loads are issued before their stores. In a
+// multi-row rectangle every in-tile offset fits 32 bits (the host caps rows per tile so that
+// (nr - 1) * max(sp, dp) + row bytes < 2^32), which keeps the per-load state small.
 template <int VB, int U>
 __device__ __forceinline__ void copy_rect(const char* __restrict__ src, char* __restrict__ dst, uint32_t nr,
                                           uint32_t vpr, uint64_t sp, uint64_t dp) {
@@ -116,17 +117,18 @@ __device__ __forceinline__ void copy_rect(const char* __restrict__ src, char* __
     }
     return;
   }
+  const uint32_t sp32 = (uint32_t)sp, dp32 = (uint32_t)dp;
   for (uint32_t base = threadIdx.x; base < total; base += stride * U) {
     V v[U];
-    uint64_t doff[U];
+    uint32_t doff[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const uint32_t i = base + u * stride;
       if (i < total) {
         const uint32_t r = i / vpr;
-        const uint32_t c = i - r * vpr;
-        v[u] = load_vec(reinterpret_cast<const V*>(src + r * sp + (uint64_t)c * VB));
-        doff[u] = r * dp + (uint64_t)c * VB;
+        const uint32_t cb = (i - r * vpr) * VB;
+        v[u] = load_vec(reinterpret_cast<const V*>(src + (r * sp32 + cb)));
+        doff[u] = r * dp32 + cb;
       }
     }
 #pragma unroll
@@ -137,36 +139,65 @@ __device__ __forceinline__ void copy_rect(const char* __restrict__ src, char* __
   }
 }
 
-__global__ void __launch_bounds__(kBlock) rs_copy_kernel(const DevSeg* __restrict__ segs, int32_t nseg, uint64_t ntiles) {
-  for (uint64_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
-    // Entry owning tile t: the last one whose tile_begin <= t.
-    int32_t lo = 0, hi = nseg - 1;
-    while (lo < hi) {
-      const int32_t mid = (lo + hi + 1) >> 1;
-      if (segs[mid].tile_begin <= t) lo = mid; else hi = mid - 1;
+// Persistent CTAs: CTA b copies tiles b, b + grid, b + 2 grid, ... so every CTA gets a share of
+// every part of the table (local and remote entries alike). Tile indices only grow, so the owning
+// entry is found by one binary search for the first tile and a forward walk afterwards.
+template <int BLOCK, int U, int MINB>
+__global__ void __launch_bounds__(BLOCK, MINB) rs_copy_kernel(const DevSeg* __restrict__ segs, int32_t nseg, uint64_t ntiles) {
+  uint64_t t = blockIdx.x;
+  if (t >= ntiles) return;
+  int32_t lo = 0, hi = nseg - 1;
+  while (lo < hi) {
+    const int32_t mid = (lo + hi + 1) >> 1;
+    if (segs[mid].tile_begin <= t) lo = mid; else hi = mid - 1;
+  }
+  int32_t si = lo;
+  uint64_t next_begin = (si + 1 < nseg) ? segs[si + 1].tile_begin : ~0ull;
+  for (; t < ntiles; t += gridDim.x) {
+    while (t >= next_begin) {
+      ++si;
+      next_begin = (si + 1 < nseg) ? segs[si + 1].tile_begin : ~0ull;
     }
-    const DevSeg s = segs[lo];
+    const DevSeg& s = segs[si];
     const uint64_t lt = t - s.tile_begin;
-    const uint64_t rg = lt / s.col_tiles;
-    const uint64_t col = lt - rg * s.col_tiles;
+    const uint32_t col_tiles = s.col_tiles;
+    const uint64_t rg = lt / col_tiles;
+    const uint64_t col = lt - rg * col_tiles;
     const uint64_t r0 = rg * s.rows_per_tile;
     const uint32_t nr = (uint32_t)min((uint64_t)s.rows_per_tile, (uint64_t)s.rows - r0);
     const uint64_t c0 = col * s.col_bytes;
     const uint64_t nb = min(s.col_bytes, s.row_bytes - c0);
-    const char* src = reinterpret_cast<const char*>(s.src) + r0 * s.src_pitch + c0;
-    char* dst = reinterpret_cast<char*>(s.dst) + r0 * s.dst_pitch + c0;
-    const uint32_t vpr = (uint32_t)(nb >> s.vshift);
-    switch (s.vshift) {
-      case 4: copy_rect<16, 4>(src, dst, nr, vpr, s.src_pitch, s.dst_pitch); break;
+    const uint64_t sp = s.src_pitch, dp = s.dst_pitch;
+    const char* src = reinterpret_cast<const char*>(s.src) + r0 * sp + c0;
+    char* dst = reinterpret_cast<char*>(s.dst) + r0 * dp + c0;
+    const uint32_t vshift = s.vshift;
+    const uint32_t vpr = (uint32_t)(nb >> vshift);
+    switch (vshift) {
+      case 4: copy_rect<16, U>(src, dst, nr, vpr, sp, dp); break;
       // Narrow widths only serve entries whose addresses or pitches are not 16-byte aligned
       // (odd shapes); one load in flight per thread keeps their register cost off the main path.
-      case 3: copy_rect<8, 1>(src, dst, nr, vpr, s.src_pitch, s.dst_pitch); break;
-      case 2: copy_rect<4, 1>(src, dst, nr, vpr, s.src_pitch, s.dst_pitch); break;
-      case 1: copy_rect<2, 1>(src, dst, nr, vpr, s.src_pitch, s.dst_pitch); break;
-      default: copy_rect<1, 1>(src, dst, nr, vpr, s.src_pitch, s.dst_pitch); break;
+      case 3: copy_rect<8, 1>(src, dst, nr, vpr, sp, dp); break;
+      case 2: copy_rect<4, 1>(src, dst, nr, vpr, sp, dp); break;
+      case 1: copy_rect<2, 1>(src, dst, nr, vpr, sp, dp); break;
+      default: copy_rect<1, 1>(src, dst, nr, vpr, sp, dp); break;
     }
   }
 }
+
+// Launch shapes (threads per CTA, 16-byte loads in flight per thread, CTAs per SM). Each keeps
+// 64 KB of loads in flight per SM. On cfg2b (1 x B200, 128 KB tiles) they span 5.83-6.00 TB/s;
+// the default (SUIKA_RS_VARIANT=2: 256 x 8 x 2) keeps two CTAs per SM to cover NVLink latency.
+struct Variant {
+  int block, unroll, min_blocks;
+  void (*fn)(const DevSeg*, int32_t, uint64_t);
+};
+const Variant kVariants[] = {
+    {512, 4, 2, rs_copy_kernel<512, 4, 2>},
+    {256, 8, 2, rs_copy_kernel<256, 8, 2>},
+    {1024, 4, 1, rs_copy_kernel<1024, 4, 1>},
+    {512, 8, 1, rs_copy_kernel<512, 8, 1>},
+};
+constexpr int kNumVariants = sizeof(kVariants) / sizeof(kVariants[0]);
 
 uint64_t env_u64(const char* name, uint64_t dflt) {
   const char* v = std::getenv(name);
@@ -194,21 +225,23 @@ int rs_copy_workspace_bytes(int64_t n_desc, uint64_t* bytes) {
   return RS_OK;
 }
 
-int rs_copy_launch(const rs_copy_desc* descs, int64_t n_desc, void* workspace_dev, uint64_t workspace_bytes, void* stream,
-                   rs_launch_info* info) {
-  if (info) std::memset(info, 0, sizeof(*info));
-  if (n_desc < 0 || (n_desc > 0 && !descs)) return efail(RS_ERR_ARG, "rs_copy_launch: bad descriptor array");
+int rs_copy_stage(const rs_copy_desc* descs, int64_t n_desc, void* workspace_dev, uint64_t workspace_bytes, void* stream,
+                  rs_launch_info* info) {
+  if (!info) return efail(RS_ERR_ARG, "rs_copy_stage: info is NULL");
+  std::memset(info, 0, sizeof(*info));
+  if (n_desc < 0 || (n_desc > 0 && !descs)) return efail(RS_ERR_ARG, "rs_copy_stage: bad descriptor array");
   const uint64_t tile_bytes = std::min<uint64_t>(1ull << 30, std::max<uint64_t>(256, env_u64("SUIKA_RS_TILE_BYTES", kDefaultTileBytes))) & ~15ull;
+  const int variant = (int)std::min<uint64_t>(env_u64("SUIKA_RS_VARIANT", 2) - 1, kNumVariants - 1);  // env value 1-based
   std::vector<DevSeg> table;
   table.reserve((size_t)n_desc);
   uint64_t ntiles = 0, total = 0;
   for (int64_t i = 0; i < n_desc; ++i) {
     const rs_copy_desc& d = descs[i];
     if (d.rows == 0 || d.row_bytes == 0) continue;
-    if (d.rows > 0xffffffffull) return efail(RS_ERR_ARG, "rs_copy_launch: entry " + std::to_string(i) + " has more than 2^32 rows");
+    if (d.rows > 0xffffffffull) return efail(RS_ERR_ARG, "rs_copy_stage: entry " + std::to_string(i) + " has more than 2^32 rows");
     if (d.rows > 1 && (d.row_bytes > d.src_pitch || d.row_bytes > d.dst_pitch))
-      return efail(RS_ERR_ARG, "rs_copy_launch: entry " + std::to_string(i) + " has rows longer than their pitch");
-    if (!d.src_dev || !d.dst_dev) return efail(RS_ERR_ARG, "rs_copy_launch: entry " + std::to_string(i) + " has a NULL address");
+      return efail(RS_ERR_ARG, "rs_copy_stage: entry " + std::to_string(i) + " has rows longer than their pitch");
+    if (!d.src_dev || !d.dst_dev) return efail(RS_ERR_ARG, "rs_copy_stage: entry " + std::to_string(i) + " has a NULL address");
     DevSeg s;
     s.src = d.src_dev;
     s.dst = d.dst_dev;
@@ -226,36 +259,60 @@ int rs_copy_launch(const rs_copy_desc* descs, int64_t n_desc, void* workspace_de
     } else {
       s.col_bytes = d.row_bytes;
       s.col_tiles = 1;
-      s.rows_per_tile = (uint32_t)std::max<uint64_t>(1, tile_bytes / d.row_bytes);
+      // Whole rows per tile, capped so that every in-tile offset fits 32 bits.
+      const uint64_t pitch = std::max(d.src_pitch, d.dst_pitch);
+      const uint64_t rows_32 = pitch ? (0xffffffffull - d.row_bytes) / pitch + 1 : 1;
+      s.rows_per_tile = (uint32_t)std::max<uint64_t>(1, std::min<uint64_t>(tile_bytes / d.row_bytes, rows_32));
       ntiles += (d.rows + s.rows_per_tile - 1) / s.rows_per_tile;
     }
     total += d.rows * d.row_bytes;
     table.push_back(s);
   }
+  info->n_entries = (int64_t)table.size();
+  info->n_tiles = ntiles;
+  info->total_bytes = total;
+  info->variant = variant;
   if (table.empty()) return RS_OK;
-  if (table.size() > 0x7fffffffull) return efail(RS_ERR_ARG, "rs_copy_launch: too many entries");
+  if (table.size() > 0x7fffffffull) return efail(RS_ERR_ARG, "rs_copy_stage: too many entries");
   const uint64_t need = ((uint64_t)table.size() * sizeof(DevSeg) + 255) & ~255ull;
   if (!workspace_dev || workspace_bytes < need)
-    return efail(RS_ERR_CAPACITY, "rs_copy_launch: workspace of " + std::to_string(workspace_bytes) + " bytes, need " + std::to_string(need));
+    return efail(RS_ERR_CAPACITY, "rs_copy_stage: workspace of " + std::to_string(workspace_bytes) + " bytes, need " + std::to_string(need));
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  // Pageable source: the runtime copies the table out before returning, so it may be freed.
   cudaError_t e = cudaMemcpyAsync(workspace_dev, table.data(), table.size() * sizeof(DevSeg), cudaMemcpyHostToDevice, st);
-  if (e != cudaSuccess) return cuda_fail(e, "rs_copy_launch: staging the copy table");
+  if (e != cudaSuccess) return cuda_fail(e, "rs_copy_stage: staging the copy table");
   int dev = 0, sms = 0, per_sm = 0;
+  const Variant& v = kVariants[variant];
   if ((e = cudaGetDevice(&dev)) != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
-  if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rs_copy_kernel, kBlock, 0)) != cudaSuccess)
+  if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, v.fn, v.block, 0)) != cudaSuccess)
     return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
-  per_sm = (int)std::min<uint64_t>((uint64_t)std::max(per_sm, 1), env_u64("SUIKA_RS_CTAS_PER_SM", 4));
-  const uint64_t grid = std::min<uint64_t>(ntiles, (uint64_t)sms * (uint64_t)per_sm);
-  rs_copy_kernel<<<(unsigned)grid, kBlock, 0, st>>>(reinterpret_cast<const DevSeg*>(workspace_dev), (int32_t)table.size(), ntiles);
-  if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(e, "rs_copy_launch: kernel launch");
-  if (info) {
-    info->n_tiles = ntiles;
-    info->total_bytes = total;
-    info->grid = (int32_t)grid;
-    info->block = kBlock;
-  }
+  per_sm = (int)std::min<uint64_t>((uint64_t)std::max(per_sm, 1), env_u64("SUIKA_RS_CTAS_PER_SM", 8));
+  info->grid = (int32_t)std::min<uint64_t>(ntiles, (uint64_t)sms * (uint64_t)per_sm);
+  info->block = v.block;
   return RS_OK;
+}
+
+int rs_copy_run(const void* workspace_dev, const rs_launch_info* info, void* stream) {
+  if (!info) return efail(RS_ERR_ARG, "rs_copy_run: info is NULL");
+  if (info->n_entries == 0 || info->n_tiles == 0) return RS_OK;
+  if (!workspace_dev || info->grid <= 0 || info->variant < 0 || info->variant >= kNumVariants)
+    return efail(RS_ERR_ARG, "rs_copy_run: info does not come from rs_copy_stage");
+  const Variant& v = kVariants[info->variant];
+  v.fn<<<(unsigned)info->grid, v.block, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const DevSeg*>(workspace_dev), (int32_t)info->n_entries, info->n_tiles);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "rs_copy_run: kernel launch");
+  return RS_OK;
+}
+
+int rs_copy_launch(const rs_copy_desc* descs, int64_t n_desc, void* workspace_dev, uint64_t workspace_bytes, void* stream,
+                   rs_launch_info* info) {
+  rs_launch_info local;
+  rs_launch_info* li = info ? info : &local;
+  int rc = rs_copy_stage(descs, n_desc, workspace_dev, workspace_bytes, stream, li);
+  if (rc) return rc;
+  return rs_copy_run(workspace_dev, li, stream);
 }
 
 }  // extern "C"

@@ -144,7 +144,27 @@ int suika_rs::fail(int code, const std::string& msg) {
   return code;
 }
 
+// A piece of the interval planner, in units of the slice dim: `len` indices starting at
+// src_start of the source shard's storage go to dst_start of the target shard's storage. Whole
+// (unsliced) tensors use outer = 1, inner = numel, extents = len = 1.
+struct Piece {
+  int32_t name = -1, src_rank = -1, dst_rank = -1;
+  int64_t outer = 1, inner = 1;
+  int64_t src_extent = 1, dst_extent = 1;
+  int64_t src_start = 0, dst_start = 0, len = 1;
+  int64_t src_numel = 0;          // elements of the source shard
+  int32_t ndim = 0;
+  int64_t dst_shape[RS_MAX_DIMS] = {0};  // actual shape of the target shard
+};
+
+struct Rule {
+  int32_t n_groups = 0;
+  rs_slice_group groups[RS_MAX_GROUPS];
+};
+
 struct rs_plan {
+  int32_t mode = 0;  // 0: reference schedule (rs_plan_build), 1: interval intersection (rs_plan_build_rules)
+  std::vector<Piece> pieces;  // mode 1: per target rank, target tensor order, storage order
   std::vector<RankLayout> src, dst;
   std::vector<rs_op> ops;
   std::vector<Meta> src_meta_of_op;  // src meta per op
@@ -408,6 +428,83 @@ int copy_out(const std::vector<T>& v, T* out, int64_t capacity, const char* fn) 
   return RS_OK;
 }
 
+// Program of a plan made by rs_plan_build_rules: the pieces of `rank`, already in target storage
+// order, become one segment per piece and sub-field.
+int program_from_pieces(const rs_plan* plan, int32_t rank, const rs_subfield* subfields, int32_t n_subfields,
+                        rs_program* prog) {
+  std::map<std::tuple<int32_t, int32_t, int32_t>, int32_t> src_slot_of;
+  size_t i = 0;
+  const size_t n = plan->pieces.size();
+  while (i < n) {
+    if (plan->pieces[i].dst_rank != rank) { ++i; continue; }
+    size_t j = i;
+    while (j < n && plan->pieces[j].dst_rank == rank && plan->pieces[j].name == plan->pieces[i].name) ++j;
+    const Piece& first = plan->pieces[i];
+    int64_t numel = 1;
+    for (int k = 0; k < first.ndim; ++k) numel *= first.dst_shape[k];
+    for (int32_t f = 0; f < n_subfields; ++f) {
+      const int64_t E = subfields[f].itemsize;
+      if (subfields[f].is_meta) {
+        rs_meta_slot ms;
+        ms.name_id = first.name;
+        ms.subfield = f;
+        ms.src_rank = first.src_rank;
+        ms.first_is_self = first.src_rank == rank ? 1 : 0;
+        prog->meta.push_back(ms);
+        continue;
+      }
+      rs_dst_slot ds;
+      std::memset(&ds, 0, sizeof(ds));
+      ds.name_id = first.name;
+      ds.subfield = f;
+      ds.ndim = first.ndim;
+      for (int k = 0; k < first.ndim; ++k) ds.shape[k] = first.dst_shape[k];
+      ds.nbytes = (uint64_t)(numel * E);
+      const int32_t dslot = (int32_t)prog->dst.size();
+      prog->dst.push_back(ds);
+      for (size_t q = i; q < j; ++q) {
+        const Piece& pc = plan->pieces[q];
+        auto key = std::make_tuple(pc.src_rank, pc.name, f);
+        auto it = src_slot_of.find(key);
+        int32_t sslot;
+        if (it == src_slot_of.end()) {
+          rs_src_slot ss;
+          std::memset(&ss, 0, sizeof(ss));
+          ss.src_rank = pc.src_rank;
+          ss.name_id = pc.name;
+          ss.subfield = f;
+          ss.nbytes = (uint64_t)(pc.src_numel * E);
+          sslot = (int32_t)prog->src.size();
+          prog->src.push_back(ss);
+          src_slot_of.emplace(key, sslot);
+        } else {
+          sslot = it->second;
+        }
+        rs_segment sg;
+        std::memset(&sg, 0, sizeof(sg));
+        sg.src_slot = sslot;
+        sg.dst_slot = dslot;
+        sg.rows = (uint64_t)pc.outer;
+        sg.row_bytes = (uint64_t)(pc.len * pc.inner * E);
+        sg.src_pitch = (uint64_t)(pc.src_extent * pc.inner * E);
+        sg.dst_pitch = (uint64_t)(pc.dst_extent * pc.inner * E);
+        sg.src_offset = (uint64_t)(pc.src_start * pc.inner * E);
+        sg.dst_offset = (uint64_t)(pc.dst_start * pc.inner * E);
+        if (sg.rows == 1 || (sg.src_pitch == sg.row_bytes && sg.dst_pitch == sg.row_bytes)) {
+          sg.row_bytes *= sg.rows;
+          sg.rows = 1;
+          sg.src_pitch = sg.dst_pitch = sg.row_bytes;
+        }
+        const uint64_t bytes = sg.rows * sg.row_bytes;
+        if (pc.src_rank == rank) prog->local_bytes += bytes; else prog->remote_bytes += bytes;
+        if (bytes > 0) prog->segs.push_back(sg);
+      }
+    }
+    i = j;
+  }
+  return RS_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -422,6 +519,15 @@ int rs_program_build(const rs_plan* plan, int32_t rank, const rs_subfield* subfi
   rs_program* prog = new (std::nothrow) rs_program();
   if (!prog) return fail(RS_ERR_ARG, "rs_program_build: out of host memory");
   try {
+    if (plan->mode == 1) {
+      int rc = program_from_pieces(plan, rank, subfields, n_subfields, prog);
+      if (rc) {
+        delete prog;
+        return rc;
+      }
+      *out = prog;
+      return RS_OK;
+    }
     // Group this rank's ops by target tensor, tensors in first-op order (the creation order of
     // target_state_dict entries, migration.py:431-433).
     std::vector<int32_t> names;
@@ -589,6 +695,49 @@ int rs_program_segments(const rs_program* p, rs_segment* o, int64_t c) {
 }
 void rs_program_free(rs_program* prog) { delete prog; }
 
+}  // extern "C"
+
+namespace {
+int resolve_segments(const rs_program* prog, int32_t src_rank, const uint64_t* src_dev, const uint64_t* src_extent,
+                     const uint64_t* dst_dev, const uint64_t* dst_extent, rs_copy_desc* out, int64_t capacity, int64_t* n_out) {
+  int64_t k = 0;
+  for (size_t i = 0; i < prog->segs.size(); ++i) {
+    const rs_segment& s = prog->segs[i];
+    if (src_rank >= 0 && prog->src[s.src_slot].src_rank != src_rank) continue;
+    if (k >= capacity) return fail(RS_ERR_CAPACITY, "rs_program_resolve: capacity too small");
+    // last byte touched = offset + (rows - 1) * pitch + row_bytes, computed without overflow.
+    const unsigned __int128 send = (unsigned __int128)s.src_offset + (unsigned __int128)(s.rows - 1) * s.src_pitch + s.row_bytes;
+    const unsigned __int128 dend = (unsigned __int128)s.dst_offset + (unsigned __int128)(s.rows - 1) * s.dst_pitch + s.row_bytes;
+    if (s.row_bytes > s.src_pitch || s.row_bytes > s.dst_pitch || send > src_extent[s.src_slot] || dend > dst_extent[s.dst_slot])
+      return fail(RS_ERR_BOUNDS, "rs_program_resolve: segment " + std::to_string(i) + " leaves its source or target (src slot " +
+                                     std::to_string(s.src_slot) + " extent " + std::to_string(src_extent[s.src_slot]) + ", dst slot " +
+                                     std::to_string(s.dst_slot) + " extent " + std::to_string(dst_extent[s.dst_slot]) + ")");
+    if (!src_dev[s.src_slot] || !dst_dev[s.dst_slot])
+      return fail(RS_ERR_ARG, "rs_program_resolve: NULL address for segment " + std::to_string(i));
+    rs_copy_desc& c = out[k++];
+    c.src_dev = src_dev[s.src_slot] + s.src_offset;
+    c.dst_dev = dst_dev[s.dst_slot] + s.dst_offset;
+    c.rows = s.rows;
+    c.row_bytes = s.row_bytes;
+    c.src_pitch = s.src_pitch;
+    c.dst_pitch = s.dst_pitch;
+  }
+  if (n_out) *n_out = k;
+  return RS_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int rs_program_resolve_from(const rs_program* prog, int32_t src_rank, const uint64_t* src_dev, const uint64_t* src_extent,
+                            const uint64_t* dst_dev, const uint64_t* dst_extent, rs_copy_desc* out, int64_t capacity,
+                            int64_t* n_out) {
+  if (!prog || src_rank < 0) return fail(RS_ERR_ARG, "rs_program_resolve_from: bad argument");
+  if (!prog->segs.empty() && (!src_dev || !src_extent || !dst_dev || !dst_extent || (!out && capacity > 0)))
+    return fail(RS_ERR_ARG, "rs_program_resolve_from: NULL argument");
+  return resolve_segments(prog, src_rank, src_dev, src_extent, dst_dev, dst_extent, out, capacity, n_out);
+}
+
 // Bind slots to addresses; every segment is bounds-checked against its slot extents.
 int rs_program_resolve(const rs_program* prog, const uint64_t* src_dev, const uint64_t* src_extent,
                        const uint64_t* dst_dev, const uint64_t* dst_extent, rs_copy_desc* out, int64_t capacity) {
@@ -615,6 +764,215 @@ int rs_program_resolve(const rs_program* prog, const uint64_t* src_dev, const ui
     c.src_pitch = s.src_pitch;
     c.dst_pitch = s.dst_pitch;
   }
+  return RS_OK;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------------------------
+// Interval planner (rs_plan_build_rules): layouts beyond the reference's contiguous chunks.
+// ---------------------------------------------------------------------------------------------
+namespace {
+
+struct Span {
+  int64_t lo, hi;   // full-tensor coordinates along the slice dim
+  int64_t at;       // storage position of lo inside the shard
+};
+
+// Slice-dim intervals held by a shard, in storage order.
+int shard_spans(const Meta& m, int d, const Rule* rule, std::vector<Span>& out) {
+  out.clear();
+  const int64_t F = m.shape[d];
+  if (!m.is_tp()) {
+    out.push_back({0, F, 0});
+    return RS_OK;
+  }
+  const int64_t i = m.tp_index, T = m.tp_deg;
+  if (!rule || rule->n_groups == 0) {
+    if (F % T) return fail(RS_ERR_SHAPE, "slice dim extent not divisible by tp degree: " + meta_str(m));
+    out.push_back({i * F / T, (i + 1) * F / T, 0});
+    return RS_OK;
+  }
+  int64_t at = 0;
+  for (int g = 0; g < rule->n_groups; ++g) {
+    const rs_slice_group& G = rule->groups[g];
+    if (G.units <= 0 || G.size <= 0 || G.size % G.units || G.offset < 0 || G.offset + G.size > F)
+      return fail(RS_ERR_SHAPE, "malformed slice rule group for " + meta_str(m));
+    const int64_t usz = G.size / G.units;
+    int64_t u0, nu;
+    if (G.units >= T) {
+      if (G.units % T) return fail(RS_ERR_SHAPE, "group units not divisible by tp degree: " + meta_str(m));
+      nu = G.units / T;
+      u0 = i * nu;
+    } else {
+      if (T % G.units) return fail(RS_ERR_SHAPE, "tp degree not a multiple of group units: " + meta_str(m));
+      nu = 1;
+      u0 = i * G.units / T;
+    }
+    out.push_back({G.offset + u0 * usz, G.offset + (u0 + nu) * usz, at});
+    at += nu * usz;
+  }
+  return RS_OK;
+}
+
+int64_t spans_extent(const std::vector<Span>& v) {
+  int64_t e = 0;
+  for (const Span& s : v) e += s.hi - s.lo;
+  return e;
+}
+
+}  // namespace
+
+extern "C" {
+
+int rs_plan_build_rules(const rs_rank_layout* src, int32_t n_src, const rs_rank_layout* dst, int32_t n_dst,
+                        const rs_slice_rule* rules, int32_t n_rules, const rs_plan_opts* opts, rs_plan** out) {
+  if (!out) return fail(RS_ERR_ARG, "rs_plan_build_rules: out is NULL");
+  *out = nullptr;
+  if (n_rules < 0 || (n_rules > 0 && !rules)) return fail(RS_ERR_ARG, "rs_plan_build_rules: bad rule array");
+  rs_plan* plan = new (std::nothrow) rs_plan();
+  if (!plan) return fail(RS_ERR_ARG, "rs_plan_build_rules: out of host memory");
+  plan->mode = 1;
+  plan->order = RS_ORDER_SEMANTIC;
+  try {
+    int rc = load_layout(src, n_src, plan->src, "source layout");
+    if (rc) { delete plan; return rc; }
+    rc = load_layout(dst, n_dst, plan->dst, "target layout");
+    if (rc) { delete plan; return rc; }
+    std::unordered_map<int32_t, Rule> rule_of;
+    for (int32_t r = 0; r < n_rules; ++r) {
+      if (rules[r].n_groups < 0 || rules[r].n_groups > RS_MAX_GROUPS)
+        return fail_and_free(plan, RS_ERR_ARG, "rs_plan_build_rules: a rule has more than RS_MAX_GROUPS groups");
+      Rule R;
+      R.n_groups = rules[r].n_groups;
+      for (int g = 0; g < R.n_groups; ++g) R.groups[g] = rules[r].groups[g];
+      rule_of[rules[r].name_id] = R;
+    }
+    (void)opts;  // the interval planner always writes slice order and balances replicas
+    int32_t max_rank = 0;
+    for (const RankLayout& L : plan->src) max_rank = std::max(max_rank, L.rank);
+    std::vector<double> egress((size_t)max_rank + 1, 0.0);
+    std::vector<Span> dspans, sspans;
+    struct Owner { int32_t rank; const Meta* meta; std::vector<Span> spans; };
+    std::vector<Owner> owners;
+    for (const RankLayout& D : plan->dst) {
+      for (const Meta& dm : D.tensors) {
+        auto rit = rule_of.find(dm.name);
+        const Rule* rule = rit == rule_of.end() ? nullptr : &rit->second;
+        owners.clear();
+        for (const RankLayout& S : plan->src) {
+          auto it = S.by_name.find(dm.name);
+          if (it != S.by_name.end()) owners.push_back({S.rank, &S.tensors[it->second], {}});
+        }
+        if (owners.empty())
+          return fail_and_free(plan, RS_ERR_NO_OWNER, "target param " + meta_str(dm) + " of rank " + std::to_string(D.rank) +
+                                                         " is not present in any source");
+        // The working dim: the target's slice dim, else any source's; all TP metas must agree.
+        int d = -1;
+        int32_t raw_dim = RS_NO_SLICE;
+        auto take_dim = [&](const Meta& m) -> bool {
+          if (!m.is_tp()) return true;
+          if (raw_dim == RS_NO_SLICE) { raw_dim = m.slice_dim; d = m.norm_dim(); return true; }
+          return m.norm_dim() == d;
+        };
+        if (!take_dim(dm)) return fail_and_free(plan, RS_ERR_SLICE_DIM, "slice dim mismatch for " + meta_str(dm));
+        for (const Owner& o : owners)
+          if (!take_dim(*o.meta) || o.meta->ndim != dm.ndim)
+            return fail_and_free(plan, RS_ERR_SLICE_DIM, "slice dim mismatch between " + meta_str(*o.meta) + " and " + meta_str(dm));
+        for (const Owner& o : owners)
+          for (int k = 0; k < dm.ndim; ++k)
+            if (o.meta->shape[k] != dm.shape[k])
+              return fail_and_free(plan, RS_ERR_SHAPE, "full shape mismatch between " + meta_str(*o.meta) + " and " + meta_str(dm));
+        Piece base;
+        base.name = dm.name;
+        base.dst_rank = D.rank;
+        base.ndim = dm.ndim;
+        for (int k = 0; k < dm.ndim; ++k) base.dst_shape[k] = dm.shape[k];
+        if (d < 0) {  // replicated everywhere: whole-tensor copies
+          base.inner = dm.full_numel();
+          base.src_numel = base.inner;
+          int32_t best = -1;
+          for (const Owner& o : owners)
+            if (o.rank == D.rank) best = o.rank;
+          if (best < 0)
+            for (const Owner& o : owners)
+              if (best < 0 || egress[o.rank] < egress[best]) best = o.rank;
+          base.src_rank = best;
+          egress[best] += (double)base.inner * dm.itemsize;
+          plan->pieces.push_back(base);
+          continue;
+        }
+        for (int k = 0; k < d; ++k) base.outer *= dm.shape[k];
+        for (int k = d + 1; k < dm.ndim; ++k) base.inner *= dm.shape[k];
+        rc = shard_spans(dm, d, rule, dspans);
+        if (rc) { delete plan; return rc; }
+        base.dst_extent = spans_extent(dspans);
+        base.dst_shape[d] = base.dst_extent;
+        for (Owner& o : owners) {
+          rc = shard_spans(*o.meta, d, rule, o.spans);
+          if (rc) { delete plan; return rc; }
+        }
+        for (const Span& ds : dspans) {
+          int64_t a = ds.lo;
+          while (a < ds.hi) {
+            // Owners holding index a, and how far each holds it contiguously (within this span).
+            int64_t b = ds.hi;
+            for (const Owner& o : owners)
+              for (const Span& sp : o.spans) {
+                if (sp.lo > a && sp.lo < b) b = sp.lo;  // another owner's span starts inside: cut there
+                if (sp.lo <= a && a < sp.hi && sp.hi < b) b = sp.hi;
+              }
+            int32_t best = -1;
+            const Owner* bo = nullptr;
+            const Span* bs = nullptr;
+            for (const Owner& o : owners)
+              for (const Span& sp : o.spans)
+                if (sp.lo <= a && b <= sp.hi) {
+                  const bool self = o.rank == D.rank;
+                  if (best < 0 || (self && best != D.rank) ||
+                      (best != D.rank && !self && egress[o.rank] < egress[best])) {
+                    best = o.rank; bo = &o; bs = &sp;
+                  }
+                }
+            if (best < 0)
+              return fail_and_free(plan, RS_ERR_NO_OWNER, "no source holds slice [" + std::to_string(a) + ", " + std::to_string(b) +
+                                                             ") of " + meta_str(dm) + " for rank " + std::to_string(D.rank));
+            Piece pc = base;
+            pc.src_rank = best;
+            pc.src_extent = spans_extent(bo->spans);
+            pc.src_numel = pc.outer * pc.src_extent * pc.inner;
+            pc.src_start = bs->at + (a - bs->lo);
+            pc.dst_start = ds.at + (a - ds.lo);
+            pc.len = b - a;
+            egress[best] += (double)(pc.outer * pc.len * pc.inner * dm.itemsize);
+            Piece* prev = plan->pieces.empty() ? nullptr : &plan->pieces.back();
+            if (prev && prev->dst_rank == pc.dst_rank && prev->name == pc.name && prev->src_rank == pc.src_rank &&
+                prev->src_start + prev->len == pc.src_start && prev->dst_start + prev->len == pc.dst_start) {
+              prev->len += pc.len;  // contiguous in both shards: one piece
+            } else {
+              plan->pieces.push_back(pc);
+            }
+            a = b;
+          }
+        }
+      }
+    }
+    // One rs_op per piece, for inspection (numel = elements of the piece).
+    for (const Piece& pc : plan->pieces) {
+      rs_op op;
+      std::memset(&op, 0, sizeof(op));
+      op.name_id = pc.name;
+      op.src_rank = pc.src_rank;
+      op.dst_rank = pc.dst_rank;
+      op.src_slice_dim = op.dst_slice_dim = RS_NO_SLICE;
+      op.src_tp_deg = op.dst_tp_deg = 1;
+      op.numel = pc.outer * pc.len * pc.inner;
+      plan->ops.push_back(op);
+    }
+  } catch (const std::exception& e) {
+    return fail_and_free(plan, RS_ERR_ARG, std::string("rs_plan_build_rules: ") + e.what());
+  }
+  *out = plan;
   return RS_OK;
 }
 

@@ -42,6 +42,7 @@ class ModelSpec:
     qkv_bias: bool = False
     pos_emb: int = 0     # learned position embedding rows (wpe); not present in the reference's models
     vocab_parallel_wte: bool = False  # slice wte on dim 0 (the reference replicates it)
+    fused_qkv: bool = False  # one qkv_proj [(nh + 2 nkv) * hd, h], TP-split by head (not in the reference)
 
     @property
     def kv_heads(self) -> int:
@@ -59,7 +60,11 @@ def layer_tensors(spec: ModelSpec, i: int) -> List[Tuple[str, Tuple[int, ...], S
     if spec.family == "llama":
         q, kv = spec.n_heads * spec.hd, spec.kv_heads * spec.hd
         out = []
-        for proj, rows in (("q_proj", q), ("k_proj", kv), ("v_proj", kv)):
+        if spec.fused_qkv:
+            out.append((p + "self_attn.qkv_proj.weight", (q + 2 * kv, h), 0))
+            if spec.qkv_bias:
+                out.append((p + "self_attn.qkv_proj.bias", (q + 2 * kv,), 0))
+        for proj, rows in (() if spec.fused_qkv else (("q_proj", q), ("k_proj", kv), ("v_proj", kv))):
             out.append((p + f"self_attn.{proj}.weight", (rows, h), 0))
             if spec.qkv_bias:
                 out.append((p + f"self_attn.{proj}.bias", (rows,), 0))
@@ -82,6 +87,19 @@ def layer_tensors(spec: ModelSpec, i: int) -> List[Tuple[str, Tuple[int, ...], S
             (p + "mlp.c_proj.linear.weight", (h, f), -1), (p + "mlp.c_proj.linear.bias", (h,), None),
         ]
     raise ValueError(f"unknown family {spec.family}")
+
+
+def qkv_rule(spec: ModelSpec) -> List[Tuple[int, int, int]]:
+    """Slice rule of a fused QKV weight/bias split by head: groups Q, K, V along dim 0, each
+    (offset, size, units=heads); KV heads are replicated when TP exceeds their count."""
+    q, kv = spec.n_heads * spec.hd, spec.kv_heads * spec.hd
+    return [(0, q, spec.n_heads), (q, kv, spec.kv_heads), (q + kv, kv, spec.kv_heads)]
+
+
+def tensor_rule(spec: ModelSpec, name: str):
+    if spec.fused_qkv and ".self_attn.qkv_proj." in name:
+        return qkv_rule(spec)
+    return None
 
 
 def first_stage_tensors(spec: ModelSpec):
@@ -138,6 +156,9 @@ def mesh_layout(spec: ModelSpec, mesh: Sequence[Sequence[Sequence[int]]], dtype:
                 for name, shape, sd in tensors:
                     tpm = None if sd is None else (sd, j, tp)
                     metas[name] = TensorMeta(name=name, dtype=dtype, shape=shape, tp_meta=tpm)
+                    rule = tensor_rule(spec, name)
+                    if rule is not None and tpm is not None:
+                        metas[name].tp_rule = rule
                 if rank in per_rank:
                     raise ValueError(f"rank {rank} appears twice in the mesh")
                 per_rank[rank] = metas
@@ -206,6 +227,37 @@ CONFIGS: Dict[str, ReshardConfig] = {
     "cfg5": ReshardConfig("cfg5", SPECS["qwen2-7b"], _m([[0, 1, 2, 3]], [[4, 5, 6, 7]]),
                           _m([[0, 1], [2, 3]], [[4, 5], [6, 7]]), "Qwen2-7B TP4xPP2 -> TP2xPP2xDP2"),
 }
+
+
+def shard_spans(full_shape: Sequence[int], tp_meta, rule=None) -> List[Tuple[int, int]]:
+    """[lo, hi) intervals of the slice dim a shard holds, in storage order: the contiguous chunk
+    of the reference, or, with a rule, each group's units (see rs_slice_rule in the C header)."""
+    if tp_meta is None:
+        return []
+    d, i, g = tp_meta
+    F = int(full_shape[d])
+    if not rule:
+        return [(i * F // g, (i + 1) * F // g)]
+    out = []
+    for off, size, units in rule:
+        usz = size // units
+        if units >= g:
+            nu = units // g
+            u0 = i * nu
+        else:
+            nu, u0 = 1, i * units // g
+        out.append((off + u0 * usz, off + (u0 + nu) * usz))
+    return out
+
+
+def actual_shape(m) -> Tuple[int, ...]:
+    """Shape of the shard a meta describes (TensorMeta.actual_shape, extended to slice rules)."""
+    shape = [int(s) for s in m.shape]
+    if m.tp_meta is not None:
+        d = m.tp_meta[0]
+        spans = shard_spans(shape, m.tp_meta, getattr(m, "tp_rule", None))
+        shape[d] = sum(hi - lo for lo, hi in spans)
+    return tuple(shape)
 
 
 def scaled_spec(spec: ModelSpec, **overrides) -> ModelSpec:

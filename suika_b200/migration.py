@@ -174,8 +174,10 @@ assert META_SLOT_DTYPE.itemsize == C.sizeof(L.RsMetaSlot)
 assert OP_DTYPE.itemsize == C.sizeof(L.RsOp)
 
 
-def _flatten_layout(layout: Dict[int, Dict[str, Any]], name_ids: Dict[str, int], names: List[str]):
-    """ParamLayout.layout -> (rank array, per-rank TENSOR_META arrays) in dict order."""
+def _flatten_layout(layout: Dict[int, Dict[str, Any]], name_ids: Dict[str, int], names: List[str],
+                    rules: Optional[Dict[str, Any]] = None):
+    """ParamLayout.layout -> (rank array, per-rank TENSOR_META arrays) in dict order. Slice rules
+    (a `tp_rule` attribute on a meta: [(offset, size, units), ...]) are collected into `rules`."""
     ranks, arrays = [], []
     for rank, metas in layout.items():
         arr = np.zeros(len(metas), dtype=L.TENSOR_META_DTYPE)
@@ -184,6 +186,11 @@ def _flatten_layout(layout: Dict[int, Dict[str, Any]], name_ids: Dict[str, int],
             if nid is None:
                 nid = name_ids[name] = len(names)
                 names.append(name)
+            rule = getattr(m, "tp_rule", None)
+            if rule is not None and rules is not None:
+                rule = tuple(tuple(int(x) for x in g) for g in rule)
+                if rules.setdefault(name, rule) != rule:
+                    raise ValueError(f"{name}: different slice rules in the source and target layouts")
             shape = tuple(int(s) for s in m.shape)
             if len(shape) > L.RS_MAX_DIMS:
                 raise ValueError(f"{name}: more than {L.RS_MAX_DIMS} dims")
@@ -220,23 +227,41 @@ class Plan:
     """
 
     def __init__(self, source_param_layout, target_param_layout, order: str = "reference",
-                 src_choice: str = "reference", minimum_est_peers: Optional[int] = None):
+                 src_choice: str = "reference", minimum_est_peers: Optional[int] = None, mode: str = "auto"):
         self._lib = L.load()
         self._h = None
-        self.order = order
         self.spl, self.tpl = source_param_layout, target_param_layout
         self.names: List[str] = []
         self.name_ids: Dict[str, int] = {}
-        s_ranks, s_arr = _flatten_layout(source_param_layout.layout, self.name_ids, self.names)
-        d_ranks, d_arr = _flatten_layout(target_param_layout.layout, self.name_ids, self.names)
+        rules: Dict[str, Any] = {}
+        s_ranks, s_arr = _flatten_layout(source_param_layout.layout, self.name_ids, self.names, rules)
+        d_ranks, d_arr = _flatten_layout(target_param_layout.layout, self.name_ids, self.names, rules)
         self.src_ranks, self.dst_ranks = s_ranks, d_ranks
+        # "reference": the reference's schedule and cat order (chunk layouts only). "interval": slice
+        # intersection, slice order, balanced replicas (any slice rules). "auto": interval iff rules.
+        self.mode = ("interval" if rules else "reference") if mode == "auto" else mode
+        self.order = order if self.mode == "reference" else "semantic"
         opts = L.RsPlanOpts()
         opts.minimum_est_peers = (1 if is_ib_enabled() else 2) if minimum_est_peers is None else int(minimum_est_peers)
-        opts.order = _ORDERS[order]
+        opts.order = _ORDERS[self.order]
         opts.src_choice = _CHOICES[src_choice]
         h = C.c_void_p()
-        L.check(self._lib.rs_plan_build(_rank_layouts(s_ranks, s_arr), len(s_ranks), _rank_layouts(d_ranks, d_arr),
-                                        len(d_ranks), C.byref(opts), C.byref(h)))
+        if self.mode == "reference":
+            if rules:
+                raise ValueError("slice rules need mode='interval' (the reference only cuts contiguous chunks)")
+            L.check(self._lib.rs_plan_build(_rank_layouts(s_ranks, s_arr), len(s_ranks), _rank_layouts(d_ranks, d_arr),
+                                            len(d_ranks), C.byref(opts), C.byref(h)))
+        else:
+            rr = (L.RsSliceRule * max(1, len(rules)))()
+            for k, (name, groups) in enumerate(rules.items()):
+                if len(groups) > L.RS_MAX_GROUPS:
+                    raise ValueError(f"{name}: more than {L.RS_MAX_GROUPS} slice groups")
+                rr[k].name_id = self.name_ids[name]
+                rr[k].n_groups = len(groups)
+                for g, (off, size, units) in enumerate(groups):
+                    rr[k].groups[g].offset, rr[k].groups[g].size, rr[k].groups[g].units = off, size, units
+            L.check(self._lib.rs_plan_build_rules(_rank_layouts(s_ranks, s_arr), len(s_ranks), _rank_layouts(d_ranks, d_arr),
+                                                  len(d_ranks), rr, len(rules), C.byref(opts), C.byref(h)))
         self._h = h
         n = C.c_int64()
         L.check(self._lib.rs_plan_num_ops(self._h, C.byref(n)))
@@ -322,27 +347,45 @@ class Program:
         return out
 
 
+class PreparedCopies:
+    """A copy table staged on the device once (rs_copy_stage) and launched any number of times
+    (rs_copy_run), each launch one sm_100a kernel. The addresses in the table must stay valid."""
+
+    def __init__(self, descs: np.ndarray, device: torch.device, stream: Optional[torch.cuda.Stream] = None):
+        self._lib = L.load()
+        self.device = device
+        self.info = L.RsLaunchInfo()
+        descs = np.ascontiguousarray(descs, dtype=L.COPY_DESC_DTYPE)
+        ws_bytes = C.c_uint64()
+        L.check(self._lib.rs_copy_workspace_bytes(len(descs), C.byref(ws_bytes)))
+        self.workspace = torch.empty(max(int(ws_bytes.value), 256), dtype=torch.uint8, device=device)
+        stream = self._stream(stream)
+        L.check(self._lib.rs_copy_stage(descs.ctypes.data, len(descs), self.workspace.data_ptr(), self.workspace.numel(),
+                                        C.c_void_p(stream.cuda_stream), C.byref(self.info)))
+
+    def _stream(self, stream):
+        current = torch.cuda.current_stream(self.device)
+        if stream is None:
+            return current
+        if stream != current:
+            stream.wait_stream(current)  # sources, targets and staging were produced on the current stream
+            self.workspace.record_stream(stream)
+        return stream
+
+    def launch(self, stream: Optional[torch.cuda.Stream] = None) -> L.RsLaunchInfo:
+        stream = self._stream(stream)
+        L.check(self._lib.rs_copy_run(self.workspace.data_ptr(), C.byref(self.info), C.c_void_p(stream.cuda_stream)))
+        return self.info
+
+
 def launch_copies(descs: np.ndarray, device: torch.device, stream: Optional[torch.cuda.Stream] = None) -> L.RsLaunchInfo:
-    """Run a COPY_DESC table with one sm_100a kernel launch on `stream` (asynchronous)."""
-    lib = L.load()
-    info = L.RsLaunchInfo()
-    n = len(descs)
-    if n == 0:
-        return info
-    descs = np.ascontiguousarray(descs, dtype=L.COPY_DESC_DTYPE)
-    ws_bytes = C.c_uint64()
-    L.check(lib.rs_copy_workspace_bytes(n, C.byref(ws_bytes)))
-    ws = torch.empty(int(ws_bytes.value), dtype=torch.uint8, device=device)
-    current = torch.cuda.current_stream(device)
-    if stream is None:
-        stream = current
-    elif stream != current:
-        stream.wait_stream(current)  # sources, targets and staging were produced on the current stream
-        ws.record_stream(stream)
-    # The workspace goes back to the stream-ordered caching allocator after the launch, so it is
-    # reused only by work queued behind this kernel.
-    L.check(lib.rs_copy_launch(descs.ctypes.data, n, ws.data_ptr(), ws.numel(), C.c_void_p(stream.cuda_stream), C.byref(info)))
-    return info
+    """Stage a COPY_DESC table and run it with one sm_100a kernel launch on `stream` (asynchronous).
+    The workspace returns to the stream-ordered caching allocator afterwards, so it is reused only
+    by work queued behind this kernel."""
+    if len(descs) == 0:
+        return L.RsLaunchInfo()
+    p = PreparedCopies(descs, device, stream)
+    return p.launch(stream)
 
 
 # ---------------------------------------------------------------------------------------------
@@ -519,11 +562,12 @@ def reshard_local(source_param_layout, target_param_layout, source_state_dicts: 
                      for n in _name_order(plan, rank)}
     md, stage = meta.descs()
     table = np.concatenate(tables + [md]) if (tables or len(md)) else np.zeros(0, dtype=L.COPY_DESC_DTYPE)
-    info = launch_copies(table, device, stream)
+    prepared = PreparedCopies(table, device, stream) if len(table) else None
+    info = prepared.launch(stream) if prepared is not None else L.RsLaunchInfo()
     if stage is not None and stream is not None:
         stage.record_stream(stream)
     if return_info:
-        return out, info, table
+        return out, info, prepared
     return out
 
 
@@ -636,6 +680,7 @@ class RankTransfer:
         self.table = np.zeros(0, dtype=L.COPY_DESC_DTYPE)
         self.remote_bytes = self.local_bytes = 0
         self._stage = None
+        self.prepared = None
         self.peers = _PeerMaps()
         if not np.any(ops["dst_rank"] == rank):
             return
@@ -680,6 +725,7 @@ class RankTransfer:
                 ent.setdefault(name, {})[s] = x
             md, self._stage = meta.descs()
             self.table = np.concatenate([table, md])
+            self.prepared = PreparedCopies(self.table, device)
             self.remote_bytes, self.local_bytes = prog.remote_bytes, prog.local_bytes
             self.target = {plan.names[n]: {s: ent[plan.names[n]][s] for s in subs if s in ent[plan.names[n]]}
                            for n in _name_order(plan, rank)}
@@ -688,8 +734,10 @@ class RankTransfer:
             raise
 
     def launch(self, stream: Optional[torch.cuda.Stream] = None) -> L.RsLaunchInfo:
-        """Queue this rank's pulls (asynchronous; one kernel launch)."""
-        return launch_copies(self.table, self.device, stream)
+        """Queue this rank's pulls (asynchronous; one kernel launch over the staged table)."""
+        if self.prepared is None:
+            return L.RsLaunchInfo()
+        return self.prepared.launch(stream)
 
     def finish(self) -> Dict[str, Dict[str, torch.Tensor]]:
         """Wait for this rank's kernel, then for every rank (barrier); release peers and sources."""
@@ -699,18 +747,184 @@ class RankTransfer:
         finally:
             self.peers.close()
         self._stage = None
+        self.prepared = None
         self.source_state_dict.clear()
         self.log(f"suika_b200: rank {self.rank} pulled {self.remote_bytes} B from peers and {self.local_bytes} B "
                  f"locally with {len(self.table)} copies")
         return self.target
 
 
+def _arena_layout(dst_slots: np.ndarray):
+    """256-byte aligned offsets of a rank's target slots inside one arena: (offsets, sizes, total)."""
+    nb = dst_slots["nbytes"].astype(np.uint64)
+    off = np.zeros(len(nb), np.uint64)
+    if len(nb) > 1:
+        off[1:] = np.cumsum((nb[:-1] + np.uint64(255)) // np.uint64(256) * np.uint64(256))
+    total = int(off[-1] + nb[-1]) if len(nb) else 0
+    return off, nb, total
+
+
+def _push_table(prog: Program, rank: int, src_addr: Callable[[str, str], Tuple[int, int]], dst_base: int,
+                dst_off: np.ndarray, dst_nb: np.ndarray, subs: Sequence[str]) -> np.ndarray:
+    """COPY_DESC entries of `prog` (a target rank's program) whose source lives on `rank`, with
+    targets at dst_base + dst_off[slot]; src_addr(name, sub) -> (address, bytes) of a local source."""
+    src_ptr = np.zeros(len(prog.src_slots), np.uint64)
+    src_ext = np.zeros(len(prog.src_slots), np.uint64)
+    for i, ss in enumerate(prog.src_slots):
+        if int(ss["src_rank"]) == rank:
+            src_ptr[i], src_ext[i] = src_addr(prog.plan.names[int(ss["name_id"])], subs[int(ss["subfield"])])
+    dst_ptr = np.asarray(dst_off, np.uint64) + np.uint64(dst_base)
+    out = np.zeros(len(prog.segments), dtype=L.COPY_DESC_DTYPE)
+    n = C.c_int64()
+    arrs = [np.ascontiguousarray(a, dtype=np.uint64) for a in (src_ptr, src_ext, dst_ptr, dst_nb)]
+    L.check(L.load().rs_program_resolve_from(prog._h, rank, *[a.ctypes.data for a in arrs], out.ctypes.data, len(out), C.byref(n)))
+    return out[: n.value]
+
+
+class RankTransferPush:
+    """One rank's share of a reshard with targets written by their sources (same contract as
+    RankTransfer: prepare / launch / finish, same targets byte for byte).
+
+    prepare: one all_gather_object shares sub-field dtypes and singleton values; every target
+    rank allocates its targets in ONE arena (returned tensors are views of it) and exports it;
+    a second all_gather_object shares the arena handles and slot offsets; each rank maps the
+    arenas of the ranks it sends to and binds a table of the pieces it is the source of (its own
+    targets' pieces included), plus the singleton values of its own targets.
+    launch: one kernel writes every piece this rank sources: local HBM reads, stores into peer
+    HBM over NVLink (posted writes, no read requests on the reverse direction).
+    finish: after this rank's kernel has finished, a barrier; past it every rank's pieces have
+    landed, and the arena mappings are closed.
+    """
+
+    def __init__(self, plan: Plan, source_state_dict: Dict[str, Dict[str, torch.Tensor]], expected_sub_fields,
+                 device: torch.device, world: Optional[dist.ProcessGroup] = None, log_func: Optional[Callable] = None):
+        self.plan, self.device, self.world = plan, device, world
+        self.source_state_dict = source_state_dict
+        self.log = log_func or (lambda m: None)
+        self.rank = rank = dist.get_rank(world)
+        ws = dist.get_world_size(world)
+        subs = [s for s, _ in expected_sub_fields]
+        sidx = {s: i for i, s in enumerate(subs)}
+        ops = plan.op_array
+        # 1. dtypes and the singleton values targets on other ranks take from this rank
+        mask = (ops["src_rank"] == rank) & (ops["dst_rank"] != rank)
+        meta_vals = {}
+        for nid in np.unique(ops["name_id"][mask]):
+            name = plan.names[int(nid)]
+            if name not in source_state_dict:
+                raise AssertionError(f"[{rank}]: param missing in source {name}")
+            for s, ft in expected_sub_fields:
+                if _is_meta_field(ft):
+                    v = source_state_dict[name][s]
+                    meta_vals[(int(nid), sidx[s])] = (v.detach().reshape(-1).cpu().view(torch.uint8).numpy().tobytes(), str(v.dtype), tuple(v.shape))
+        my_dtypes = {s: str(d).replace("torch.", "") for s, d in _sub_dtypes(expected_sub_fields, [source_state_dict]).items()}
+        torch.cuda.current_stream(device).synchronize()  # sources are complete before this rank's kernel reads them
+        g1: List[Any] = [None] * ws
+        dist.all_gather_object(g1, {"meta": meta_vals, "dtypes": my_dtypes}, group=world)
+        dtypes: Dict[str, torch.dtype] = {}
+        for g in g1:
+            for s, d in g["dtypes"].items():
+                dtypes.setdefault(s, getattr(torch, d))
+        spec = _program_spec(expected_sub_fields, dtypes)
+        # 2. this rank's targets, in one exported arena
+        self.peers = _PeerMaps()
+        self.target: Dict[str, Dict[str, torch.Tensor]] = {}
+        self.remote_bytes = self.local_bytes = 0
+        self.prepared = None
+        self._stage = None
+        my_prog = plan.program(rank, spec) if np.any(ops["dst_rank"] == rank) else None
+        arena_handle, arena_offset, slot_off, slot_nb = None, 0, np.zeros(0, np.uint64), np.zeros(0, np.uint64)
+        dst_views = []
+        if my_prog is not None and len(my_prog.dst_slots):
+            slot_off, slot_nb, total = _arena_layout(my_prog.dst_slots)
+            self.arena = torch.empty(max(total, 1), dtype=torch.uint8, device=device)
+            for ds, o, nb in zip(my_prog.dst_slots, slot_off, slot_nb):
+                shape = tuple(int(x) for x in ds["shape"][: ds["ndim"]])
+                dt = dtypes[subs[ds["subfield"]]]
+                dst_views.append(self.arena[int(o):int(o) + int(nb)].view(dt).view(shape))
+            # the handle covers the whole allocation holding the arena; peers add the arena's offset
+            hs, where = _export([self.arena])
+            arena_handle, arena_offset = hs[0], where[0][1]
+        g2: List[Any] = [None] * ws
+        dist.all_gather_object(g2, {"arena": arena_handle, "arena_offset": arena_offset, "off": slot_off, "nb": slot_nb},
+                               group=world)
+        try:
+            # 3. the pieces this rank sources, for every target rank
+            tables = []
+            targets = sorted(set(int(t) for t in ops["dst_rank"][ops["src_rank"] == rank]))
+            def src_addr(name, sub):
+                if name not in source_state_dict:
+                    raise AssertionError(f"[{rank}]: param missing in source {name}")
+                v = _check_source(source_state_dict[name][sub], name, sub, device, dtypes[sub])
+                source_state_dict[name][sub] = v
+                return v.data_ptr(), v.numel() * v.element_size()
+
+            for T in targets:
+                prog = my_prog if T == rank else plan.program(T, spec)
+                base = self.arena.data_ptr() if T == rank else self.peers.base(T, 0, g2[T]["arena"]) + g2[T]["arena_offset"]
+                d = _push_table(prog, rank, src_addr, base, g2[T]["off"], g2[T]["nb"], subs)
+                nbytes = int((d["rows"] * d["row_bytes"]).sum())
+                if T == rank:
+                    self.local_bytes += nbytes
+                else:
+                    self.remote_bytes += nbytes
+                tables.append(d)
+            # 4. this rank's targets: dict in the reference's order, singleton values staged locally
+            if my_prog is not None:
+                ent: Dict[str, Dict[str, torch.Tensor]] = {}
+                for ds, x in zip(my_prog.dst_slots, dst_views):
+                    ent.setdefault(plan.names[ds["name_id"]], {})[subs[ds["subfield"]]] = x
+                meta = _MetaStage(device)
+                for ms in my_prog.meta_slots:
+                    nid, sf, sr = int(ms["name_id"]), int(ms["subfield"]), int(ms["src_rank"])
+                    name, s = plan.names[nid], subs[sf]
+                    if sr == rank:
+                        v = source_state_dict[name][s]
+                    else:
+                        raw, dt, shape = g1[sr]["meta"][(nid, sf)]
+                        v = torch.frombuffer(bytearray(raw), dtype=torch.uint8).view(getattr(torch, dt.replace("torch.", ""))).reshape(shape)
+                    x = _meta_target(v, bool(ms["first_is_self"]), expected_sub_fields[sf][1], device)
+                    meta.add(v, x)
+                    ent.setdefault(name, {})[s] = x
+                md, self._stage = meta.descs()
+                tables.append(md)
+                self.target = {plan.names[n]: {s: ent[plan.names[n]][s] for s in subs if s in ent[plan.names[n]]}
+                               for n in _name_order(plan, rank)}
+            self.table = np.concatenate(tables) if tables else np.zeros(0, dtype=L.COPY_DESC_DTYPE)
+            if len(self.table):
+                self.prepared = PreparedCopies(self.table, device)
+        except BaseException:
+            self.peers.close()
+            raise
+
+    def launch(self, stream: Optional[torch.cuda.Stream] = None) -> L.RsLaunchInfo:
+        """Queue this rank's writes (asynchronous; one kernel launch over the staged table)."""
+        if self.prepared is None:
+            return L.RsLaunchInfo()
+        return self.prepared.launch(stream)
+
+    def finish(self) -> Dict[str, Dict[str, torch.Tensor]]:
+        """Wait for this rank's kernel, then for every rank (barrier): all pieces have landed."""
+        try:
+            torch.cuda.current_stream(self.device).synchronize()
+            dist.barrier(group=self.world)
+        finally:
+            self.peers.close()
+        self._stage = None
+        self.prepared = None
+        self.source_state_dict.clear()
+        self.log(f"suika_b200: rank {self.rank} wrote {self.remote_bytes} B to peers and {self.local_bytes} B locally")
+        return self.target
+
+
 def execute_plan_distributed(plan: Plan, source_state_dict: Dict[str, Dict[str, torch.Tensor]], expected_sub_fields,
                              device: torch.device, world: Optional[dist.ProcessGroup] = None,
-                             log_func: Optional[Callable] = None, timers: Optional[dict] = None):
+                             log_func: Optional[Callable] = None, timers: Optional[dict] = None, direction: str = "pull"):
     """Run one rank's share of a reshard (execute_param_transfer, migration.py:397-556): prepare,
-    one kernel launch, finish (see RankTransfer). Collective over `world`."""
-    rt = RankTransfer(plan, source_state_dict, expected_sub_fields, device, world, log_func)
+    one kernel launch, finish. Collective over `world`. direction="pull": each target rank reads
+    its pieces (RankTransfer); "push": each source rank writes them (RankTransferPush)."""
+    cls = {"pull": RankTransfer, "push": RankTransferPush}[direction]
+    rt = cls(plan, source_state_dict, expected_sub_fields, device, world, log_func)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record()
     info = rt.launch()
@@ -725,7 +939,7 @@ def execute_plan_distributed(plan: Plan, source_state_dict: Dict[str, Dict[str, 
 
 def schedule_and_execute_param_transfer(source_param_layout, target_param_layout, source_state_dict: Dict[str, Dict[str, torch.Tensor]],
                                         other_context_dict: Dict[str, Any], device, world: Optional[dist.ProcessGroup],
-                                        prof=None, forcefully_free: bool = False, log_func=None):
+                                        prof=None, forcefully_free: bool = False, log_func=None, direction: Optional[str] = None):
     """Drop-in for Suika's schedule_and_execute_param_transfer (migration.py:558-598).
 
     Same arguments, same return value ({name: {sub_field: tensor}} of this rank, tensors new and
@@ -742,7 +956,9 @@ def schedule_and_execute_param_transfer(source_param_layout, target_param_layout
     plan = Plan(source_param_layout, target_param_layout)
     prof.stop("schedule")
     prof.start("execute", require_memory=True)
-    target = execute_plan_distributed(plan, source_state_dict, other_context_dict["expected_sub_fields"], device, world, log_func)
+    direction = direction or os.environ.get("SUIKA_RESHARD_DIRECTION", "pull")
+    target = execute_plan_distributed(plan, source_state_dict, other_context_dict["expected_sub_fields"], device, world, log_func,
+                                      direction=direction)
     torch.cuda.synchronize(device=device)
     prof.stop("execute", require_memory=True)
     return target

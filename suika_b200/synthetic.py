@@ -78,11 +78,16 @@ def _contig(a: np.ndarray) -> np.ndarray:
     return a if a.flags.c_contiguous else np.ascontiguousarray(a)
 
 
-def host_shard(full: np.ndarray, tp_meta) -> np.ndarray:
+def host_shard(full: np.ndarray, tp_meta, rule=None) -> np.ndarray:
+    """The shard of a full tensor: the reference's contiguous chunk, or the spans of a slice rule."""
     if tp_meta is None or full.ndim == 0:
         return _contig(full)
     d, i, g = tp_meta
-    return np.ascontiguousarray(np.split(full, g, axis=d)[i])
+    if not rule:
+        return np.ascontiguousarray(np.split(full, g, axis=d)[i])
+    from .layouts import shard_spans
+    parts = [np.take(full, np.arange(lo, hi), axis=d) for lo, hi in shard_spans(full.shape, tp_meta, rule)]
+    return np.ascontiguousarray(np.concatenate(parts, axis=d))
 
 
 def host_states(layout, subfields=SUBFIELDS, seed: int = 0, distinct_steps: bool = False,
@@ -100,7 +105,7 @@ def host_states(layout, subfields=SUBFIELDS, seed: int = 0, distinct_steps: bool
                 key = (name, sub)
                 if key not in cache:
                     cache[key] = host_full(name, sub, m.shape, seed, distinct_steps)
-                ent[sub] = cache[key] if sub == "step" else host_shard(cache[key], m.tp_meta)
+                ent[sub] = cache[key] if sub == "step" else host_shard(cache[key], m.tp_meta, getattr(m, "tp_rule", None))
             rs[name] = ent
         out[rank] = rs
     return out
@@ -133,14 +138,26 @@ def _torch_seed(seed: int, *parts) -> int:
     return int(_seed(seed, *parts).generate_state(1, dtype=np.uint64)[0] & 0x7FFFFFFFFFFFFFFF)
 
 
-def fill_device_shard(out: torch.Tensor, name: str, sub: str, tp_meta, seed: int = 0) -> None:
-    """Fill one source shard on its device (same distributions as the host generator)."""
+def fill_device_shard(out: torch.Tensor, name: str, sub: str, tp_meta, seed: int = 0, rule=None, full_shape=None) -> None:
+    """Fill one source shard on its device (same distributions as the host generator). Shards of
+    a slice rule are filled span by span, seeded by the span, so replicated units agree."""
     if sub == "step":
         out.fill_(1.0)
         return
+    if rule and tp_meta is not None:
+        from .layouts import shard_spans
+        d, at = tp_meta[0], 0
+        for lo, hi in shard_spans(full_shape, tp_meta, rule):
+            _fill(out.narrow(d, at, hi - lo), name, sub, seed, ("span", lo, hi))
+            at += hi - lo
+        return
     idx, deg = (0, 1) if tp_meta is None else (tp_meta[1], tp_meta[2])
+    _fill(out, name, sub, seed, (idx, deg))
+
+
+def _fill(out: torch.Tensor, name: str, sub: str, seed: int, key) -> None:
     g = torch.Generator(device=out.device)
-    g.manual_seed(_torch_seed(seed, name, "master" if sub == "param" else sub, idx, deg))
+    g.manual_seed(_torch_seed(seed, name, "master" if sub == "param" else sub, *key))
     if sub in ("param", "master"):
         if is_norm(name):
             out.fill_(0.0 if name.endswith(".bias") else 1.0)
@@ -148,6 +165,11 @@ def fill_device_shard(out: torch.Tensor, name: str, sub: str, tp_meta, seed: int
         tmp = torch.empty(out.shape, dtype=torch.float32, device=out.device)
         tmp.normal_(0.0, 0.02, generator=g)
         out.copy_(tmp)  # bf16 param: round-to-nearest-even of the fp32 master draw
+        return
+    if not out.is_contiguous():  # a span of a rule shard
+        tmp = torch.empty(out.shape, dtype=out.dtype, device=out.device)
+        _fill(tmp, name, sub, seed, key)
+        out.copy_(tmp)
         return
     if sub == "exp_avg":
         out.normal_(0.0, 1e-3, generator=g)
@@ -192,7 +214,7 @@ class DeviceState:
                 o = offs[(name, sub)]
                 ent[sub] = self.arenas[kind][o:o + numel].view(shape)
                 if fill:
-                    fill_device_shard(ent[sub], name, sub, m.tp_meta, seed)
+                    fill_device_shard(ent[sub], name, sub, m.tp_meta, seed, getattr(m, "tp_rule", None), m.shape)
             self.state[name] = ent
         self.kind_of = kind_of
 
@@ -201,8 +223,5 @@ class DeviceState:
 
 
 def _actual_shape(m) -> Tuple[int, ...]:
-    shape = [int(s) for s in m.shape]
-    if m.tp_meta is not None:
-        d, _, g = m.tp_meta
-        shape[d] //= g
-    return tuple(shape)
+    from .layouts import actual_shape
+    return actual_shape(m)

@@ -17,7 +17,7 @@ from tests.helpers import load_golden
 pytestmark = pytest.mark.gpu
 
 
-def _worker(rank, world, case, port, outdir):
+def _worker(rank, world, case, port, outdir, direction):
     res = {"rank": rank}
     try:
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
@@ -39,7 +39,7 @@ def _worker(rank, world, case, port, outdir):
             os.environ["NCCL_IB_DISABLE"] = "1"
         timers = {}
         plan = M.Plan(spl, tpl)
-        out = M.execute_plan_distributed(plan, src, S.expected_sub_fields(), dev, None, timers=timers)
+        out = M.execute_plan_distributed(plan, src, S.expected_sub_fields(), dev, None, timers=timers, direction=direction)
         torch.cuda.synchronize()
         assert len(src) == 0  # cleared like the reference's source_state_dict
         dig = {}
@@ -60,21 +60,22 @@ def _worker(rank, world, case, port, outdir):
         json.dump(res, f)
 
 
-def run_case(case, port):
+def run_case(case, port, direction="pull"):
     world = CASES[case]["config"].world_size
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
     with tempfile.TemporaryDirectory() as d:
-        mp.spawn(_worker, args=(world, case, port, d), nprocs=world, join=True)
+        mp.spawn(_worker, args=(world, case, port, d, direction), nprocs=world, join=True)
         return [json.load(open(os.path.join(d, f"rank{r}.json"))) for r in range(world)]
 
 
+@pytest.mark.parametrize("direction", ["pull", "push"])
 @pytest.mark.parametrize("case", ["cfg2b_mini", "odd_mini", "cfg1", "cfg2_mini", "cfg3_mini", "cfg4_mini", "cfg5_mini",
                                   "shrink_mini", "hetero_mini", "cfg2_mini_noib"])
-def test_drop_in_matches_reference(case):
+def test_drop_in_matches_reference(case, direction):
     g = load_golden(case)
-    results = run_case(case, 29800 + sorted(CASES).index(case))
+    results = run_case(case, 29800 + 2 * sorted(CASES).index(case) + (direction == "push"), direction)
     for r in results:
         assert "error" not in r, r.get("error")
     for rank_s, want in g["ranks"].items():

@@ -72,7 +72,7 @@ def test_views_move_only_row_split_pieces():
     spl, tpl = cfg.layouts()
     states = golden_states(cfg)
     dev_states = to_device(states)
-    out, info, table = M.reshard_local(spl, tpl, dev_states, S.expected_sub_fields(), DEV, views=True, return_info=True)
+    out, info, _ = M.reshard_local(spl, tpl, dev_states, S.expected_sub_fields(), DEV, views=True, return_info=True)
     torch.cuda.synchronize()
     ops = O.schedule(spl, tpl, minimum_est_peers=1)
     moved = 0
@@ -124,3 +124,24 @@ def test_copy_kernel_random_rectangles(tile, monkeypatch):
 def test_empty_table_is_a_noop():
     info = M.launch_copies(np.zeros(0, dtype=M.L.COPY_DESC_DTYPE), DEV)
     assert info.n_tiles == 0
+
+
+@pytest.mark.parametrize("case", ["cfg3_fused_mini", "gqa_rep_src", "gqa_rep_dst", "gqa_pp"])
+def test_reshard_local_extension_layouts_match_reslice(case):
+    """Fused QKV split by head, GQA KV-head replication, vocab-parallel wte (layouts the reference
+    lacks): the kernel's targets equal gathering the full tensors and re-slicing them."""
+    from tests.test_extension_layouts import EXT_CASES
+    cfg = EXT_CASES[case]
+    spl, tpl = cfg.layouts()
+    states = S.host_states(spl, SUBS, seed=3, distinct_steps=True)
+    out = M.reshard_local(spl, tpl, to_device(states), S.expected_sub_fields(), DEV)
+    torch.cuda.synchronize()
+    for rank, metas in tpl.layout.items():
+        if not metas:
+            continue
+        want = O.semantic_target(states, spl, tpl, SUB_META, rank)
+        for name, ent in want.items():
+            for sub, a in ent.items():
+                if sub == "step":
+                    continue
+                assert np.array_equal(host(out[rank][name][sub]).reshape(-1).view(np.uint8), a.reshape(-1).view(np.uint8)), (rank, name, sub)
