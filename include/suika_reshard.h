@@ -275,6 +275,25 @@ int rs_copy_launch(const rs_copy_desc* descs, int64_t n_desc,
                    void* workspace_dev, uint64_t workspace_bytes,
                    void* stream, rs_launch_info* info);
 
+/* ---- copy launch without allocation --------------------------------------------------------
+ * No counterpart in the reference. rs_copy_launch needs device workspace for its copy table.
+ * Some callers cannot allocate device memory at the moment they reshard. A live migration runs
+ * when HBM is fullest: the old and the new layout are both resident, and a framework's caching
+ * allocator may already hold the rest of the GPU, so a cudaMalloc can fail or force the
+ * allocator to release and synchronise. For them this entry point keeps its copy table in a
+ * fixed device array built into the library: at most RS_NOALLOC_MAX_ENTRIES non-empty
+ * descriptors per call (about 1.2 MB of device memory, held on every GPU that loads the library
+ * until the process exits). It calls no cudaMalloc, cudaFree or other allocating routine.
+ *   - Larger tables are rejected with RS_ERR_CAPACITY; use rs_copy_launch for them.
+ *   - The first call on a device looks up the array's device address (cudaGetSymbolAddress)
+ *     with that device current. Make that first call before any stream capture.
+ *   - Every call shares the one array and overwrites the entries it uses; nothing in it needs
+ *     to start at zero. Calls on the same stream are ordered; calls that overlap on the GPU
+ *     (different streams, or several threads) race on the array.
+ * Otherwise it behaves like rs_copy_launch: same descriptors, same kernel, asynchronous. */
+#define RS_NOALLOC_MAX_ENTRIES 16384
+int rs_copy_launch_noalloc(const rs_copy_desc* descs, int64_t n_desc, void* stream, rs_launch_info* info);
+
 /* ---- peer memory (replaces NCCL P2P connections, utils.py:212-236) ----------------------- */
 typedef struct rs_peer_handle {
   uint8_t ipc[64];          /* cudaIpcMemHandle_t of the allocation      */

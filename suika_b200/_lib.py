@@ -32,6 +32,7 @@ RS_ORDER_REFERENCE = 0
 RS_ORDER_SEMANTIC = 1
 RS_SRC_REFERENCE = 0
 RS_SRC_BALANCED = 1
+RS_NOALLOC_MAX_ENTRIES = 16384
 
 
 class RsTensorMeta(C.Structure):
@@ -144,6 +145,7 @@ SIGNATURES = {
     "rs_copy_stage": (C.c_int, [_P, C.c_int64, _P, C.c_uint64, _P, C.POINTER(RsLaunchInfo)]),
     "rs_copy_run": (C.c_int, [_P, C.POINTER(RsLaunchInfo), _P]),
     "rs_copy_launch": (C.c_int, [_P, C.c_int64, _P, C.c_uint64, _P, C.POINTER(RsLaunchInfo)]),
+    "rs_copy_launch_noalloc": (C.c_int, [_P, C.c_int64, _P, C.POINTER(RsLaunchInfo)]),
     "rs_peer_export": (C.c_int, [_P, C.POINTER(RsPeerHandle), C.POINTER(C.c_uint64)]),
     "rs_peer_open": (C.c_int, [C.POINTER(RsPeerHandle), C.POINTER(_P)]),
     "rs_peer_close": (C.c_int, [_P]),

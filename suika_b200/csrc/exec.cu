@@ -22,6 +22,7 @@
 #include <algorithm>
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 #include <string>
 #include <unistd.h>
 #include <vector>
@@ -384,6 +385,124 @@ int rs_peer_close(void* base_dev) {
   if (!base_dev) return efail(RS_ERR_ARG, "rs_peer_close: NULL argument");
   cudaError_t e = cudaIpcCloseMemHandle(base_dev);
   if (e != cudaSuccess) return cuda_fail(e, "rs_peer_close: cudaIpcCloseMemHandle");
+  return RS_OK;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------------------------
+// Copy launch that allocates nothing (rs_copy_launch_noalloc). Its copy table lives in a
+// file-scope device array instead of caller-provided workspace.
+// ---------------------------------------------------------------------------------------------
+namespace {
+
+// Every GPU that loads this library holds this array (RS_NOALLOC_MAX_ENTRIES x 72 bytes, about
+// 1.2 MB) until the process exits. All calls share it.
+static __device__ __align__(256) DevSeg g_noalloc_table[RS_NOALLOC_MAX_ENTRIES];
+
+constexpr int kMaxDevices = 64;
+// Device address of g_noalloc_table per device ordinal, set once by the first call on that device.
+DevSeg* g_noalloc_addr[kMaxDevices] = {nullptr};
+std::mutex g_noalloc_mu;
+
+int noalloc_table_addr(int dev, DevSeg** out) {
+  if (dev < 0 || dev >= kMaxDevices) return efail(RS_ERR_ARG, "rs_copy_launch_noalloc: device ordinal out of range");
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_addr[dev]) {
+    // In host code the array's name is only a stand-in; the device address has to be looked up,
+    // with the device current.
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_table);
+    if (e != cudaSuccess) return cuda_fail(e, "rs_copy_launch_noalloc: cudaGetSymbolAddress");
+    g_noalloc_addr[dev] = static_cast<DevSeg*>(p);
+  }
+  *out = g_noalloc_addr[dev];
+  return RS_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int rs_copy_launch_noalloc(const rs_copy_desc* descs, int64_t n_desc, void* stream, rs_launch_info* info) {
+  rs_launch_info local;
+  rs_launch_info* li = info ? info : &local;
+  std::memset(li, 0, sizeof(*li));
+  if (n_desc < 0 || (n_desc > 0 && !descs)) return efail(RS_ERR_ARG, "rs_copy_launch_noalloc: bad descriptor array");
+  int64_t n_entries = 0;
+  for (int64_t i = 0; i < n_desc; ++i)
+    if (descs[i].rows != 0 && descs[i].row_bytes != 0) ++n_entries;
+  if (n_entries > RS_NOALLOC_MAX_ENTRIES)
+    return efail(RS_ERR_CAPACITY, "rs_copy_launch_noalloc: " + std::to_string(n_entries) + " non-empty copies, at most " +
+                                      std::to_string(RS_NOALLOC_MAX_ENTRIES) + " fit the built-in table; use rs_copy_launch");
+  if (n_entries == 0) return RS_OK;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  DevSeg* table = nullptr;
+  int rc = noalloc_table_addr(dev, &table);
+  if (rc) return rc;
+  const uint64_t tile_bytes = std::min<uint64_t>(1ull << 30, std::max<uint64_t>(256, env_u64("SUIKA_RS_TILE_BYTES", kDefaultTileBytes))) & ~15ull;
+  const int variant = (int)std::min<uint64_t>(env_u64("SUIKA_RS_VARIANT", 2) - 1, kNumVariants - 1);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  // Stage in chunks through a stack buffer: no heap memory on the host either. Pageable copies
+  // are taken out of the buffer before cudaMemcpyAsync returns, so the buffer can be refilled.
+  constexpr int kChunk = 128;
+  DevSeg chunk[kChunk];
+  int nc = 0;
+  int64_t written = 0;
+  uint64_t ntiles = 0, total = 0;
+  for (int64_t i = 0; i < n_desc; ++i) {
+    const rs_copy_desc& d = descs[i];
+    if (d.rows == 0 || d.row_bytes == 0) continue;
+    if (d.rows > 0xffffffffull) return efail(RS_ERR_ARG, "rs_copy_launch_noalloc: entry " + std::to_string(i) + " has more than 2^32 rows");
+    if (d.rows > 1 && (d.row_bytes > d.src_pitch || d.row_bytes > d.dst_pitch))
+      return efail(RS_ERR_ARG, "rs_copy_launch_noalloc: entry " + std::to_string(i) + " has rows longer than their pitch");
+    if (!d.src_dev || !d.dst_dev) return efail(RS_ERR_ARG, "rs_copy_launch_noalloc: entry " + std::to_string(i) + " has a NULL address");
+    DevSeg& s = chunk[nc++];
+    s.src = d.src_dev;
+    s.dst = d.dst_dev;
+    s.src_pitch = d.src_pitch;
+    s.dst_pitch = d.dst_pitch;
+    s.rows = (uint32_t)d.rows;
+    s.row_bytes = d.row_bytes;
+    s.vshift = vector_shift(d);
+    s.tile_begin = ntiles;
+    if (d.row_bytes >= tile_bytes) {
+      s.col_bytes = tile_bytes;
+      s.col_tiles = (uint32_t)((d.row_bytes + tile_bytes - 1) / tile_bytes);
+      s.rows_per_tile = 1;
+      ntiles += (uint64_t)s.col_tiles * d.rows;
+    } else {
+      s.col_bytes = d.row_bytes;
+      s.col_tiles = 1;
+      const uint64_t pitch = std::max(d.src_pitch, d.dst_pitch);
+      const uint64_t rows_32 = pitch ? (0xffffffffull - d.row_bytes) / pitch + 1 : 1;
+      s.rows_per_tile = (uint32_t)std::max<uint64_t>(1, std::min<uint64_t>(tile_bytes / d.row_bytes, rows_32));
+      ntiles += (d.rows + s.rows_per_tile - 1) / s.rows_per_tile;
+    }
+    total += d.rows * d.row_bytes;
+    if (nc == kChunk || written + nc == n_entries) {
+      e = cudaMemcpyAsync(table + written, chunk, nc * sizeof(DevSeg), cudaMemcpyHostToDevice, st);
+      if (e != cudaSuccess) return cuda_fail(e, "rs_copy_launch_noalloc: staging the copy table");
+      written += nc;
+      nc = 0;
+    }
+  }
+  int sms = 0, per_sm = 0;
+  const Variant& v = kVariants[variant];
+  if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+  if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, v.fn, v.block, 0)) != cudaSuccess)
+    return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+  per_sm = (int)std::min<uint64_t>((uint64_t)std::max(per_sm, 1), env_u64("SUIKA_RS_CTAS_PER_SM", 8));
+  li->n_entries = n_entries;
+  li->n_tiles = ntiles;
+  li->total_bytes = total;
+  li->variant = variant;
+  li->grid = (int32_t)std::min<uint64_t>(ntiles, (uint64_t)sms * (uint64_t)per_sm);
+  li->block = v.block;
+  v.fn<<<(unsigned)li->grid, v.block, 0, st>>>(table, (int32_t)n_entries, ntiles);
+  if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(e, "rs_copy_launch_noalloc: kernel launch");
   return RS_OK;
 }
 
