@@ -356,34 +356,37 @@ def run_dist(args):
     exp = S.expected_sub_fields()
     plan = M.Plan(spl, tpl, minimum_est_peers=1)
     src = {n: dict(e) for n, e in state.state.items()}
-    rt = (M.RankTransfer if args.direction == "pull" else M.RankTransferPush)(plan, src, exp, dev)
+    rt = (M.RankTransfer if args.direction == "pull" else M.RankTransferPush)(plan, src, exp, dev, phased=not args.no_phases)
     its = [2, 4, 4, 4]
     rb = plan.rank_bytes(its)
     moved_all = int(plan.op_array["numel"].sum()) * sum(its)
     ingress = rb["ingress"].get(rank, 0)
     # warm-up, then K timed steps between barriers; device time per rank, max over ranks
+    # a step: every phase of the reshard (phases separated by host barriers), device time from the
+    # first launch to the end of the last kernel on this rank; the step time is the max over ranks
     with Clocks(local) as ck:
         for _ in range(args.warmup):
             dist.barrier()
-            rt.launch()
+            rt.run()
             torch.cuda.synchronize()
         dist.barrier()
         torch.cuda.synchronize()
-        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         kern = []
         for _ in range(args.steps):
             dist.barrier()
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record()
-            rt.launch()
+            rt.run()
             b.record()
             torch.cuda.synchronize()
             kern.append(a.elapsed_time(b))
         torch.cuda.synchronize()
         dist.barrier()
-    step_ms = torch.tensor([statistics.mean(kern)], dtype=torch.float64, device=dev)
-    dist.all_reduce(step_ms, op=dist.ReduceOp.MAX)
-    t = float(step_ms.item()) / 1e3
+    per_rank = [None] * world
+    dist.all_gather_object(per_rank, (round(statistics.mean(kern), 4), int(rt.remote_bytes), int(rt.local_bytes),
+                                      sum(1 for p in rt.prepared_phases if p is not None)))
+    rt_phase_counts = [p[3] for p in per_rank]
+    t = max(p[0] for p in per_rank) / 1e3  # the step ends when the slowest rank's kernel ends
     check = verify_dist(plan, rt, rank, state.state, exp) if not args.no_check else {"status": "skipped"}
     target = rt.finish()
     del target
@@ -402,14 +405,16 @@ def run_dist(args):
                        "max_ingress_gb": round(max(rb["ingress"].values(), default=0) / 1e9, 3),
                        "max_egress_gb": round(max(rb["egress"].values(), default=0) / 1e9, 3),
                        "l2": "inputs larger than L2 (no flush needed)", "order": "reference", "src_choice": "reference",
-                       "direction": args.direction},
+                       "direction": args.direction, "phases": rt.n_phases},
             "migration_s": round(t, 6),
             "nvlink_gbs_per_gpu": round(max(rb["ingress"].values(), default=0) / t / 1e9, 2),
             "roofline": {"bound": "nvlink", "achieved": round(achieved, 1), "peak": NVLINK_PEER_GBS, "unit": "GB/s",
                          "frac": round(achieved / NVLINK_PEER_GBS, 4),
                          "peak_source": "measured peer copy per direction per GPU on this pool (900 GB/s nominal)",
                          "traffic": None, "algorithmic_bytes_per_launch": int(max_dir), "kernel_ms": round(t * 1e3, 4)},
-            "gpu_launches": args.steps * world,
+            "gpu_launches": args.steps * sum(rt_phase_counts),
+            "per_rank": [{"rank": r, "kernel_ms": p[0], "remote_gb": round(p[1] / 1e9, 3), "local_gb": round(p[2] / 1e9, 3)}
+                         for r, p in enumerate(per_rank)],
             "clocks": ck.summary(),
             "check": check,
         }
@@ -549,7 +554,8 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-check", action="store_true")
-    ap.add_argument("--direction", choices=["pull", "push"], default="pull",
+    ap.add_argument("--no-phases", action="store_true", help="N > 1: run all transfers at once instead of in matching phases")
+    ap.add_argument("--direction", choices=["pull", "push"], default="push",
                     help="N > 1: target ranks read their pieces (pull) or source ranks write them (push)")
     args = ap.parse_args()
     if args.warmup < 3:

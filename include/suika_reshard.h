@@ -228,11 +228,14 @@ typedef struct rs_copy_desc {
   uint64_t row_bytes;
   uint64_t src_pitch;
   uint64_t dst_pitch;
+  uint64_t flags;      /* RS_COPY_REMOTE: source or target is another GPU's memory */
 } rs_copy_desc;
+#define RS_COPY_REMOTE 1u
 
 /* Bind the program's slots to addresses. src_dev[i]/src_extent[i]: address of src slot i and
  * the bytes readable from it; same for dst. Every segment is checked against the extents
- * (RS_ERR_BOUNDS) before it is written to out[]. Writes rs_program_counts.n_segments entries. */
+ * (RS_ERR_BOUNDS) before it is written to out[]. Writes rs_program_counts.n_segments entries;
+ * entries whose source is another rank get RS_COPY_REMOTE. */
 int rs_program_resolve(const rs_program* prog,
                        const uint64_t* src_dev, const uint64_t* src_extent,
                        const uint64_t* dst_dev, const uint64_t* dst_extent,
@@ -240,7 +243,7 @@ int rs_program_resolve(const rs_program* prog,
 
 /* Like rs_program_resolve, but only for the segments whose source slot lives on `src_rank`
  * (the pieces that rank sends when targets are written by their sources); slots of other ranks
- * may be 0. Writes *n_out entries. */
+ * may be 0. Writes *n_out entries; RS_COPY_REMOTE when the program's rank is not src_rank. */
 int rs_program_resolve_from(const rs_program* prog, int32_t src_rank,
                             const uint64_t* src_dev, const uint64_t* src_extent,
                             const uint64_t* dst_dev, const uint64_t* dst_extent,
@@ -255,6 +258,8 @@ typedef struct rs_launch_info {
   uint64_t n_tiles;        /* work units the table was cut into        */
   uint64_t total_bytes;    /* bytes copied                             */
   int64_t n_entries;       /* non-empty entries staged                 */
+  uint64_t n_tiles_remote; /* tiles of RS_COPY_REMOTE entries (staged first; every CTA interleaves them
+                              with local tiles so NVLink and HBM copies overlap) */
   int32_t grid;            /* CTAs launched                            */
   int32_t block;           /* threads per CTA                          */
   int32_t variant;         /* launch shape (SUIKA_RS_VARIANT, 1-based) */
@@ -270,6 +275,9 @@ int rs_copy_stage(const rs_copy_desc* descs, int64_t n_desc, void* workspace_dev
 /* Launch the copy kernel over a staged table (asynchronous; may be repeated while the workspace
  * and every address in the table stay valid). Synchronise the stream before reading targets. */
 int rs_copy_run(const void* workspace_dev, const rs_launch_info* info, void* stream);
+/* Status bits of the last launch over a staged table (synchronises `stream`): 0 = no error;
+ * 1 = a bounded wait inside the kernel ran out (the kernel stopped early; targets incomplete). */
+int rs_copy_status(const void* workspace_dev, const rs_launch_info* info, void* stream, uint32_t* status);
 /* rs_copy_stage + rs_copy_run. n_desc == 0 is a no-op. */
 int rs_copy_launch(const rs_copy_desc* descs, int64_t n_desc,
                    void* workspace_dev, uint64_t workspace_bytes,

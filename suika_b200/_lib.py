@@ -94,14 +94,17 @@ class RsSegment(C.Structure):
                 ("rows", C.c_uint64), ("row_bytes", C.c_uint64), ("src_pitch", C.c_uint64), ("dst_pitch", C.c_uint64)]
 
 
+RS_COPY_REMOTE = 1
+
+
 class RsCopyDesc(C.Structure):
     _fields_ = [("src_dev", C.c_uint64), ("dst_dev", C.c_uint64), ("rows", C.c_uint64), ("row_bytes", C.c_uint64),
-                ("src_pitch", C.c_uint64), ("dst_pitch", C.c_uint64)]
+                ("src_pitch", C.c_uint64), ("dst_pitch", C.c_uint64), ("flags", C.c_uint64)]
 
 
 class RsLaunchInfo(C.Structure):
-    _fields_ = [("n_tiles", C.c_uint64), ("total_bytes", C.c_uint64), ("n_entries", C.c_int64), ("grid", C.c_int32),
-                ("block", C.c_int32), ("variant", C.c_int32), ("reserved", C.c_int32)]
+    _fields_ = [("n_tiles", C.c_uint64), ("total_bytes", C.c_uint64), ("n_entries", C.c_int64), ("n_tiles_remote", C.c_uint64),
+                ("grid", C.c_int32), ("block", C.c_int32), ("variant", C.c_int32), ("reserved", C.c_int32)]
 
 
 class RsPeerHandle(C.Structure):
@@ -113,7 +116,7 @@ class RsPeerHandle(C.Structure):
 TENSOR_META_DTYPE = np.dtype([("name_id", "<i4"), ("ndim", "<i4"), ("shape", "<i8", (RS_MAX_DIMS,)),
                               ("itemsize", "<i4"), ("slice_dim", "<i4"), ("tp_index", "<i4"), ("tp_deg", "<i4")])
 COPY_DESC_DTYPE = np.dtype([("src_dev", "<u8"), ("dst_dev", "<u8"), ("rows", "<u8"), ("row_bytes", "<u8"),
-                            ("src_pitch", "<u8"), ("dst_pitch", "<u8")])
+                            ("src_pitch", "<u8"), ("dst_pitch", "<u8"), ("flags", "<u8")])
 SEGMENT_DTYPE = np.dtype([("src_slot", "<i4"), ("dst_slot", "<i4"), ("src_offset", "<u8"), ("dst_offset", "<u8"),
                           ("rows", "<u8"), ("row_bytes", "<u8"), ("src_pitch", "<u8"), ("dst_pitch", "<u8")])
 assert TENSOR_META_DTYPE.itemsize == C.sizeof(RsTensorMeta)
@@ -144,6 +147,7 @@ SIGNATURES = {
     "rs_copy_workspace_bytes": (C.c_int, [C.c_int64, C.POINTER(C.c_uint64)]),
     "rs_copy_stage": (C.c_int, [_P, C.c_int64, _P, C.c_uint64, _P, C.POINTER(RsLaunchInfo)]),
     "rs_copy_run": (C.c_int, [_P, C.POINTER(RsLaunchInfo), _P]),
+    "rs_copy_status": (C.c_int, [_P, C.POINTER(RsLaunchInfo), _P, C.POINTER(C.c_uint32)]),
     "rs_copy_launch": (C.c_int, [_P, C.c_int64, _P, C.c_uint64, _P, C.POINTER(RsLaunchInfo)]),
     "rs_copy_launch_noalloc": (C.c_int, [_P, C.c_int64, _P, C.POINTER(RsLaunchInfo)]),
     "rs_peer_export": (C.c_int, [_P, C.POINTER(RsPeerHandle), C.POINTER(C.c_uint64)]),

@@ -140,65 +140,314 @@ __device__ __forceinline__ void copy_rect(const char* __restrict__ src, char* __
   }
 }
 
-// Persistent CTAs: CTA b copies tiles b, b + grid, b + 2 grid, ... so every CTA gets a share of
-// every part of the table (local and remote entries alike). Tile indices only grow, so the owning
-// entry is found by one binary search for the first tile and a forward walk afterwards.
-template <int BLOCK, int U, int MINB>
-__global__ void __launch_bounds__(BLOCK, MINB) rs_copy_kernel(const DevSeg* __restrict__ segs, int32_t nseg, uint64_t ntiles) {
-  uint64_t t = blockIdx.x;
-  if (t >= ntiles) return;
-  int32_t lo = 0, hi = nseg - 1;
-  while (lo < hi) {
-    const int32_t mid = (lo + hi + 1) >> 1;
-    if (segs[mid].tile_begin <= t) lo = mid; else hi = mid - 1;
+// Tile scheduling shared by the kernels. The table holds the remote entries first (tiles
+// [0, n_remote)) and the local ones after them (tiles [n_remote, n_tiles)). CTA b visits tiles
+// b, b + grid, b + 2 grid, ... of each range and interleaves the two in proportion to their
+// counts, so NVLink and HBM copies overlap inside every CTA instead of running one after the
+// other. Tile indices only grow within a range, so each cursor finds its entry with one binary
+// search and a forward walk.
+struct TileCursor {
+  uint64_t t, end, next_begin;
+  int32_t si;
+  __device__ void init(const DevSeg* __restrict__ segs, int32_t nseg, uint64_t first, uint64_t end_) {
+    t = first;
+    end = end_;
+    si = 0;
+    next_begin = ~0ull;
+    if (t >= end) return;
+    int32_t lo = 0, hi = nseg - 1;
+    while (lo < hi) {
+      const int32_t mid = (lo + hi + 1) >> 1;
+      if (segs[mid].tile_begin <= t) lo = mid; else hi = mid - 1;
+    }
+    si = lo;
+    next_begin = (si + 1 < nseg) ? segs[si + 1].tile_begin : ~0ull;
   }
-  int32_t si = lo;
-  uint64_t next_begin = (si + 1 < nseg) ? segs[si + 1].tile_begin : ~0ull;
-  for (; t < ntiles; t += gridDim.x) {
+  __device__ const DevSeg& locate(const DevSeg* __restrict__ segs, int32_t nseg) {
     while (t >= next_begin) {
       ++si;
       next_begin = (si + 1 < nseg) ? segs[si + 1].tile_begin : ~0ull;
     }
-    const DevSeg& s = segs[si];
-    const uint64_t lt = t - s.tile_begin;
-    const uint32_t col_tiles = s.col_tiles;
-    const uint64_t rg = lt / col_tiles;
-    const uint64_t col = lt - rg * col_tiles;
-    const uint64_t r0 = rg * s.rows_per_tile;
-    const uint32_t nr = (uint32_t)min((uint64_t)s.rows_per_tile, (uint64_t)s.rows - r0);
-    const uint64_t c0 = col * s.col_bytes;
-    const uint64_t nb = min(s.col_bytes, s.row_bytes - c0);
-    const uint64_t sp = s.src_pitch, dp = s.dst_pitch;
-    const char* src = reinterpret_cast<const char*>(s.src) + r0 * sp + c0;
-    char* dst = reinterpret_cast<char*>(s.dst) + r0 * dp + c0;
-    const uint32_t vshift = s.vshift;
-    const uint32_t vpr = (uint32_t)(nb >> vshift);
-    switch (vshift) {
-      case 4: copy_rect<16, U>(src, dst, nr, vpr, sp, dp); break;
+    return segs[si];
+  }
+};
+
+struct Tile {
+  const char* src;
+  char* dst;
+  uint64_t sp, dp, nb;
+  uint32_t nr, vshift;
+};
+
+__device__ __forceinline__ Tile tile_of(const DevSeg& s, uint64_t t) {
+  Tile x;
+  const uint64_t lt = t - s.tile_begin;
+  const uint64_t rg = lt / s.col_tiles;
+  const uint64_t col = lt - rg * s.col_tiles;
+  const uint64_t r0 = rg * s.rows_per_tile;
+  x.nr = (uint32_t)min((uint64_t)s.rows_per_tile, (uint64_t)s.rows - r0);
+  const uint64_t c0 = col * s.col_bytes;
+  x.nb = min(s.col_bytes, s.row_bytes - c0);
+  x.sp = s.src_pitch;
+  x.dp = s.dst_pitch;
+  x.src = reinterpret_cast<const char*>(s.src) + r0 * x.sp + c0;
+  x.dst = reinterpret_cast<char*>(s.dst) + r0 * x.dp + c0;
+  x.vshift = s.vshift;
+  return x;
+}
+
+struct Schedule {
+  TileCursor rc, lc;
+  uint64_t n_r, n_l, d_r, d_l;
+  __device__ void init(const DevSeg* __restrict__ segs, int32_t nseg, uint64_t ntiles, uint64_t nremote) {
+    const uint64_t b = blockIdx.x, g = gridDim.x;
+    rc.init(segs, nseg, b, nremote);
+    lc.init(segs, nseg, nremote + b, ntiles);
+    n_r = nremote > b ? (nremote - b + g - 1) / g : 0;
+    n_l = ntiles - nremote > b ? (ntiles - nremote - b + g - 1) / g : 0;
+    d_r = d_l = 0;
+  }
+  __device__ bool next(const DevSeg* __restrict__ segs, int32_t nseg, Tile& out) {
+    const bool hr = d_r < n_r, hl = d_l < n_l;
+    if (!hr && !hl) return false;
+    const bool take_r = hr && (!hl || d_r * n_l <= d_l * n_r);
+    TileCursor& c = take_r ? rc : lc;
+    out = tile_of(c.locate(segs, nseg), c.t);
+    c.t += gridDim.x;
+    if (take_r) ++d_r; else ++d_l;
+    return true;
+  }
+};
+
+template <int BLOCK, int U, int MINB>
+__global__ void __launch_bounds__(BLOCK, MINB) rs_copy_kernel(const DevSeg* __restrict__ segs, int32_t nseg, uint64_t ntiles,
+                                                               uint64_t nremote, uint32_t* status) {
+  (void)status;  // the vector-copy kernel has no waits that could fail
+  Schedule sch;
+  sch.init(segs, nseg, ntiles, nremote);
+  Tile x;
+  while (sch.next(segs, nseg, x)) {
+    const uint32_t vpr = (uint32_t)(x.nb >> x.vshift);
+    switch (x.vshift) {
+      case 4: copy_rect<16, U>(x.src, x.dst, x.nr, vpr, x.sp, x.dp); break;
       // Narrow widths only serve entries whose addresses or pitches are not 16-byte aligned
       // (odd shapes); one load in flight per thread keeps their register cost off the main path.
-      case 3: copy_rect<8, 1>(src, dst, nr, vpr, sp, dp); break;
-      case 2: copy_rect<4, 1>(src, dst, nr, vpr, sp, dp); break;
-      case 1: copy_rect<2, 1>(src, dst, nr, vpr, sp, dp); break;
-      default: copy_rect<1, 1>(src, dst, nr, vpr, sp, dp); break;
+      case 3: copy_rect<8, 1>(x.src, x.dst, x.nr, vpr, x.sp, x.dp); break;
+      case 2: copy_rect<4, 1>(x.src, x.dst, x.nr, vpr, x.sp, x.dp); break;
+      case 1: copy_rect<2, 1>(x.src, x.dst, x.nr, vpr, x.sp, x.dp); break;
+      default: copy_rect<1, 1>(x.src, x.dst, x.nr, vpr, x.sp, x.dp); break;
     }
   }
 }
 
-// Launch shapes (threads per CTA, 16-byte loads in flight per thread, CTAs per SM). Each keeps
-// 64 KB of loads in flight per SM. On cfg2b (1 x B200, 128 KB tiles) they span 5.83-6.00 TB/s;
-// the default (SUIKA_RS_VARIANT=2: 256 x 8 x 2) keeps two CTAs per SM to cover NVLink latency.
+// ---------------------------------------------------------------------------------------------
+// TMA variant: bulk copies through a shared-memory ring.
+// One warp per CTA. Lane 0 cuts the CTA's tiles into row chunks (16-byte aligned entries only),
+// packs them into 16 KB stages, loads a stage with cp.async.bulk (global -> shared, completing
+// on the stage's mbarrier) and writes it out with cp.async.bulk (shared -> global). LOOKAHEAD
+// stages are in flight at once. Entries that are not 16-byte aligned are copied by the whole warp
+// with vector loads. Every mbarrier wait is bounded by %globaltimer: past the limit the kernel
+// sets kStatusWaitTimeout in *status, drains what it issued (bounded again) and stops.
+// ---------------------------------------------------------------------------------------------
+constexpr uint32_t kStatusWaitTimeout = 1u;
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t phase) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred P;\n mbarrier.try_wait.parity.shared::cta.b64 P, [%1], %2;\n selp.b32 %0, 1, 0, P;\n}"
+      : "=r"(ok) : "r"(bar), "r"(phase) : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t phase) {
+  if (mbar_try_wait(bar, phase)) return true;
+  const uint64_t t0 = global_ns();
+  while (!mbar_try_wait(bar, phase))
+    if (global_ns() - t0 > kWaitLimitNs) return false;
+  return true;
+}
+__device__ __forceinline__ void bulk_load(uint32_t smem_dst, const void* gsrc, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(smem_dst), "l"(gsrc), "r"(bytes), "r"(bar) : "memory");
+}
+__device__ __forceinline__ void bulk_store(void* gdst, uint32_t smem_src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst), "r"(smem_src), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+template <int STAGES, int STAGE_BYTES, int MAXE>
+struct TmaSmem {
+  struct Ent {
+    uint64_t src, dst;
+    uint32_t off, bytes;
+    uint64_t pad;
+  };
+  alignas(128) unsigned char buf[STAGES][STAGE_BYTES];
+  Ent ent[STAGES][MAXE];
+  uint64_t bar[STAGES];
+  uint32_t count[STAGES];
+  uint32_t bytes[STAGES];
+};
+
+template <int STAGES, int STAGE_BYTES, int MAXE, int LOOKAHEAD>
+struct TmaPipe {
+  using Smem = TmaSmem<STAGES, STAGE_BYTES, MAXE>;
+  Smem& sm;
+  uint32_t filled = 0;   // stages issued
+  uint32_t retired = 0;  // stages stored
+  bool failed = false;
+  uint32_t* status;
+
+  __device__ TmaPipe(Smem& s, uint32_t* st) : sm(s), status(st) {}
+
+  __device__ uint32_t cur() const { return filled % STAGES; }
+
+  // Chunk appended to the stage being filled; the stage is issued when full.
+  __device__ void add(const char* src, char* dst, uint32_t bytes) {
+    while (bytes > 0 && !failed) {
+      const uint32_t s = cur();
+      const uint32_t room = STAGE_BYTES - sm.bytes[s];
+      const uint32_t take = bytes < room ? bytes : room;
+      auto& e = sm.ent[s][sm.count[s]++];
+      e.src = reinterpret_cast<uint64_t>(src);
+      e.dst = reinterpret_cast<uint64_t>(dst);
+      e.off = sm.bytes[s];
+      e.bytes = take;
+      sm.bytes[s] += take;
+      src += take;
+      dst += take;
+      bytes -= take;
+      if (sm.bytes[s] == STAGE_BYTES || sm.count[s] == MAXE) issue();
+    }
+  }
+
+  __device__ void issue() {
+    const uint32_t s = cur();
+    if (sm.count[s] == 0) return;
+    if (filled - retired == LOOKAHEAD) retire();
+    if (failed) return;
+    // the buffer of stage s was last stored STAGES - LOOKAHEAD retires ago
+    bulk_wait_read<STAGES - LOOKAHEAD>();
+    const uint32_t bar = smem_u32(&sm.bar[s]);
+    mbar_arrive_expect_tx(bar, sm.bytes[s]);
+    const uint32_t base = smem_u32(&sm.buf[s][0]);
+    for (uint32_t i = 0; i < sm.count[s]; ++i) {
+      const auto& e = sm.ent[s][i];
+      bulk_load(base + e.off, reinterpret_cast<const void*>(e.src), e.bytes, bar);
+    }
+    ++filled;
+    const uint32_t n = cur();
+    sm.count[n] = 0;
+    sm.bytes[n] = 0;
+  }
+
+  __device__ void retire() {
+    const uint32_t s = retired % STAGES;
+    const uint32_t phase = (retired / STAGES) & 1u;
+    if (!mbar_wait_bounded(smem_u32(&sm.bar[s]), phase)) {
+      atomicOr(status, kStatusWaitTimeout);
+      failed = true;
+      return;
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    const uint32_t base = smem_u32(&sm.buf[s][0]);
+    for (uint32_t i = 0; i < sm.count[s]; ++i) {
+      const auto& e = sm.ent[s][i];
+      bulk_store(reinterpret_cast<void*>(e.dst), base + e.off, e.bytes);
+    }
+    bulk_commit();
+    ++retired;
+  }
+
+  __device__ void finish() {
+    if (!failed) issue();
+    while (!failed && retired < filled) retire();
+    if (failed) {  // drain the loads still in flight (bounded) before the CTA's shared memory goes away
+      for (uint32_t q = retired + 1; q < filled; ++q)
+        (void)mbar_wait_bounded(smem_u32(&sm.bar[q % STAGES]), (q / STAGES) & 1u);
+    }
+    bulk_wait_all();
+  }
+};
+
+template <int STAGES, int STAGE_BYTES, int MAXE, int LOOKAHEAD, int MINB>
+__global__ void __launch_bounds__(32, MINB) rs_copy_tma_kernel(const DevSeg* __restrict__ segs, int32_t nseg, uint64_t ntiles,
+                                                               uint64_t nremote, uint32_t* status) {
+  using Pipe = TmaPipe<STAGES, STAGE_BYTES, MAXE, LOOKAHEAD>;
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  auto& sm = *reinterpret_cast<typename Pipe::Smem*>(smem_raw);
+  const bool leader = threadIdx.x == 0;
+  if (leader) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_u32(&sm.bar[s]), 1);
+      sm.count[s] = 0;
+      sm.bytes[s] = 0;
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncwarp();
+  Pipe pipe(sm, status);
+  Schedule sch;
+  sch.init(segs, nseg, ntiles, nremote);
+  Tile x;
+  while (sch.next(segs, nseg, x)) {
+    if (x.vshift == 4) {
+      if (leader && !pipe.failed)
+        for (uint32_t r = 0; r < x.nr; ++r) pipe.add(x.src + r * x.sp, x.dst + r * x.dp, (uint32_t)x.nb);
+      continue;
+    }
+    const uint32_t vpr = (uint32_t)(x.nb >> x.vshift);
+    switch (x.vshift) {
+      case 3: copy_rect<8, 1>(x.src, x.dst, x.nr, vpr, x.sp, x.dp); break;
+      case 2: copy_rect<4, 1>(x.src, x.dst, x.nr, vpr, x.sp, x.dp); break;
+      case 1: copy_rect<2, 1>(x.src, x.dst, x.nr, vpr, x.sp, x.dp); break;
+      default: copy_rect<1, 1>(x.src, x.dst, x.nr, vpr, x.sp, x.dp); break;
+    }
+  }
+  if (leader) pipe.finish();
+}
+
+// Launch shapes. Vector-copy variants: (threads per CTA, 16-byte loads in flight per thread, CTAs
+// per SM), each with 64 KB of loads in flight per SM; on cfg2b (1 x B200, 128 KB tiles) they span
+// 5.83-6.00 TB/s. TMA variants: one warp per CTA, (stages, stage bytes, stages in flight, CTAs per
+// SM). The default (SUIKA_RS_VARIANT=2: 256 x 8 x 2) keeps two CTAs per SM.
 struct Variant {
   int block, unroll, min_blocks;
-  void (*fn)(const DevSeg*, int32_t, uint64_t);
+  size_t smem;
+  void (*fn)(const DevSeg*, int32_t, uint64_t, uint64_t, uint32_t*);
 };
+using TmaA = TmaSmem<8, 16384, 32>;
+using TmaB = TmaSmem<6, 16384, 32>;
+using TmaC = TmaSmem<12, 16384, 32>;
 const Variant kVariants[] = {
-    {512, 4, 2, rs_copy_kernel<512, 4, 2>},
-    {256, 8, 2, rs_copy_kernel<256, 8, 2>},
-    {1024, 4, 1, rs_copy_kernel<1024, 4, 1>},
-    {512, 8, 1, rs_copy_kernel<512, 8, 1>},
+    {512, 4, 2, 0, rs_copy_kernel<512, 4, 2>},
+    {256, 8, 2, 0, rs_copy_kernel<256, 8, 2>},
+    {1024, 4, 1, 0, rs_copy_kernel<1024, 4, 1>},
+    {512, 8, 1, 0, rs_copy_kernel<512, 8, 1>},
+    {32, 0, 1, sizeof(TmaA), rs_copy_tma_kernel<8, 16384, 32, 6, 1>},
+    {32, 0, 2, sizeof(TmaB), rs_copy_tma_kernel<6, 16384, 32, 4, 2>},
+    {32, 0, 1, sizeof(TmaC), rs_copy_tma_kernel<12, 16384, 32, 10, 1>},
 };
 constexpr int kNumVariants = sizeof(kVariants) / sizeof(kVariants[0]);
+
+// Workspace layout: the staged table, then a 256-byte status block (word 0: kStatus* bits).
+constexpr uint64_t kStatusBytes = 256;
+uint64_t status_offset(int64_t n_entries) { return ((uint64_t)n_entries * sizeof(DevSeg) + 255) & ~255ull; }
 
 uint64_t env_u64(const char* name, uint64_t dflt) {
   const char* v = std::getenv(name);
@@ -216,13 +465,47 @@ uint32_t vector_shift(const rs_copy_desc& d) {
   return s;
 }
 
+// One descriptor -> one table entry (validated), its tiles numbered from `ntiles`.
+int make_entry(const rs_copy_desc& d, int64_t i, uint64_t tile_bytes, uint64_t& ntiles, DevSeg& s, const char* fn) {
+  if (d.rows > 0xffffffffull) return efail(RS_ERR_ARG, std::string(fn) + ": entry " + std::to_string(i) + " has more than 2^32 rows");
+  if (d.rows > 1 && (d.row_bytes > d.src_pitch || d.row_bytes > d.dst_pitch))
+    return efail(RS_ERR_ARG, std::string(fn) + ": entry " + std::to_string(i) + " has rows longer than their pitch");
+  if (!d.src_dev || !d.dst_dev) return efail(RS_ERR_ARG, std::string(fn) + ": entry " + std::to_string(i) + " has a NULL address");
+  s.src = d.src_dev;
+  s.dst = d.dst_dev;
+  s.src_pitch = d.src_pitch;
+  s.dst_pitch = d.dst_pitch;
+  s.rows = (uint32_t)d.rows;
+  s.row_bytes = d.row_bytes;
+  s.vshift = vector_shift(d);
+  s.tile_begin = ntiles;
+  if (d.row_bytes >= tile_bytes) {
+    s.col_bytes = tile_bytes;
+    s.col_tiles = (uint32_t)((d.row_bytes + tile_bytes - 1) / tile_bytes);
+    s.rows_per_tile = 1;
+    ntiles += (uint64_t)s.col_tiles * d.rows;
+  } else {
+    s.col_bytes = d.row_bytes;
+    s.col_tiles = 1;
+    // Whole rows per tile, capped so that every in-tile offset fits 32 bits.
+    const uint64_t pitch = std::max(d.src_pitch, d.dst_pitch);
+    const uint64_t rows_32 = pitch ? (0xffffffffull - d.row_bytes) / pitch + 1 : 1;
+    s.rows_per_tile = (uint32_t)std::max<uint64_t>(1, std::min<uint64_t>(tile_bytes / d.row_bytes, rows_32));
+    ntiles += (d.rows + s.rows_per_tile - 1) / s.rows_per_tile;
+  }
+  return RS_OK;
+}
+
+bool empty_desc(const rs_copy_desc& d) { return d.rows == 0 || d.row_bytes == 0; }
+bool remote_desc(const rs_copy_desc& d) { return (d.flags & RS_COPY_REMOTE) != 0; }
+
 }  // namespace
 
 extern "C" {
 
 int rs_copy_workspace_bytes(int64_t n_desc, uint64_t* bytes) {
   if (!bytes || n_desc < 0) return efail(RS_ERR_ARG, "rs_copy_workspace_bytes: bad argument");
-  *bytes = ((uint64_t)n_desc * sizeof(DevSeg) + 255) & ~255ull;
+  *bytes = (((uint64_t)n_desc * sizeof(DevSeg) + 255) & ~255ull) + kStatusBytes;
   return RS_OK;
 }
 
@@ -235,58 +518,43 @@ int rs_copy_stage(const rs_copy_desc* descs, int64_t n_desc, void* workspace_dev
   const int variant = (int)std::min<uint64_t>(env_u64("SUIKA_RS_VARIANT", 2) - 1, kNumVariants - 1);  // env value 1-based
   std::vector<DevSeg> table;
   table.reserve((size_t)n_desc);
-  uint64_t ntiles = 0, total = 0;
-  for (int64_t i = 0; i < n_desc; ++i) {
-    const rs_copy_desc& d = descs[i];
-    if (d.rows == 0 || d.row_bytes == 0) continue;
-    if (d.rows > 0xffffffffull) return efail(RS_ERR_ARG, "rs_copy_stage: entry " + std::to_string(i) + " has more than 2^32 rows");
-    if (d.rows > 1 && (d.row_bytes > d.src_pitch || d.row_bytes > d.dst_pitch))
-      return efail(RS_ERR_ARG, "rs_copy_stage: entry " + std::to_string(i) + " has rows longer than their pitch");
-    if (!d.src_dev || !d.dst_dev) return efail(RS_ERR_ARG, "rs_copy_stage: entry " + std::to_string(i) + " has a NULL address");
-    DevSeg s;
-    s.src = d.src_dev;
-    s.dst = d.dst_dev;
-    s.src_pitch = d.src_pitch;
-    s.dst_pitch = d.dst_pitch;
-    s.rows = (uint32_t)d.rows;
-    s.row_bytes = d.row_bytes;
-    s.vshift = vector_shift(d);
-    s.tile_begin = ntiles;
-    if (d.row_bytes >= tile_bytes) {
-      s.col_bytes = tile_bytes;
-      s.col_tiles = (uint32_t)((d.row_bytes + tile_bytes - 1) / tile_bytes);
-      s.rows_per_tile = 1;
-      ntiles += (uint64_t)s.col_tiles * d.rows;
-    } else {
-      s.col_bytes = d.row_bytes;
-      s.col_tiles = 1;
-      // Whole rows per tile, capped so that every in-tile offset fits 32 bits.
-      const uint64_t pitch = std::max(d.src_pitch, d.dst_pitch);
-      const uint64_t rows_32 = pitch ? (0xffffffffull - d.row_bytes) / pitch + 1 : 1;
-      s.rows_per_tile = (uint32_t)std::max<uint64_t>(1, std::min<uint64_t>(tile_bytes / d.row_bytes, rows_32));
-      ntiles += (d.rows + s.rows_per_tile - 1) / s.rows_per_tile;
+  uint64_t ntiles = 0, total = 0, nremote = 0;
+  for (int pass = 0; pass < 2; ++pass) {  // remote entries first, then local ones
+    for (int64_t i = 0; i < n_desc; ++i) {
+      const rs_copy_desc& d = descs[i];
+      if (empty_desc(d) || remote_desc(d) != (pass == 0)) continue;
+      DevSeg sg;
+      const int rc = make_entry(d, i, tile_bytes, ntiles, sg, "rs_copy_stage");
+      if (rc) return rc;
+      total += d.rows * d.row_bytes;
+      table.push_back(sg);
     }
-    total += d.rows * d.row_bytes;
-    table.push_back(s);
+    if (pass == 0) nremote = ntiles;
   }
   info->n_entries = (int64_t)table.size();
   info->n_tiles = ntiles;
+  info->n_tiles_remote = nremote;
   info->total_bytes = total;
   info->variant = variant;
   if (table.empty()) return RS_OK;
   if (table.size() > 0x7fffffffull) return efail(RS_ERR_ARG, "rs_copy_stage: too many entries");
-  const uint64_t need = ((uint64_t)table.size() * sizeof(DevSeg) + 255) & ~255ull;
+  const uint64_t need = status_offset((int64_t)table.size()) + kStatusBytes;
   if (!workspace_dev || workspace_bytes < need)
     return efail(RS_ERR_CAPACITY, "rs_copy_stage: workspace of " + std::to_string(workspace_bytes) + " bytes, need " + std::to_string(need));
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   // Pageable source: the runtime copies the table out before returning, so it may be freed.
   cudaError_t e = cudaMemcpyAsync(workspace_dev, table.data(), table.size() * sizeof(DevSeg), cudaMemcpyHostToDevice, st);
   if (e != cudaSuccess) return cuda_fail(e, "rs_copy_stage: staging the copy table");
+  e = cudaMemsetAsync(static_cast<char*>(workspace_dev) + status_offset((int64_t)table.size()), 0, kStatusBytes, st);
+  if (e != cudaSuccess) return cuda_fail(e, "rs_copy_stage: clearing the status block");
   int dev = 0, sms = 0, per_sm = 0;
   const Variant& v = kVariants[variant];
   if ((e = cudaGetDevice(&dev)) != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
-  if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, v.fn, v.block, 0)) != cudaSuccess)
+  if (v.smem > 0 &&
+      (e = cudaFuncSetAttribute(v.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)v.smem)) != cudaSuccess)
+    return cuda_fail(e, "rs_copy_stage: cudaFuncSetAttribute");
+  if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, v.fn, v.block, v.smem)) != cudaSuccess)
     return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
   per_sm = (int)std::min<uint64_t>((uint64_t)std::max(per_sm, 1), env_u64("SUIKA_RS_CTAS_PER_SM", 8));
   info->grid = (int32_t)std::min<uint64_t>(ntiles, (uint64_t)sms * (uint64_t)per_sm);
@@ -300,10 +568,26 @@ int rs_copy_run(const void* workspace_dev, const rs_launch_info* info, void* str
   if (!workspace_dev || info->grid <= 0 || info->variant < 0 || info->variant >= kNumVariants)
     return efail(RS_ERR_ARG, "rs_copy_run: info does not come from rs_copy_stage");
   const Variant& v = kVariants[info->variant];
-  v.fn<<<(unsigned)info->grid, v.block, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      reinterpret_cast<const DevSeg*>(workspace_dev), (int32_t)info->n_entries, info->n_tiles);
+  uint32_t* status = reinterpret_cast<uint32_t*>(static_cast<char*>(const_cast<void*>(workspace_dev)) + status_offset(info->n_entries));
+  v.fn<<<(unsigned)info->grid, v.block, v.smem, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const DevSeg*>(workspace_dev), (int32_t)info->n_entries, info->n_tiles, info->n_tiles_remote, status);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "rs_copy_run: kernel launch");
+  return RS_OK;
+}
+
+int rs_copy_status(const void* workspace_dev, const rs_launch_info* info, void* stream, uint32_t* status) {
+  if (!info || !status) return efail(RS_ERR_ARG, "rs_copy_status: NULL argument");
+  *status = 0;
+  if (info->n_entries == 0) return RS_OK;
+  if (!workspace_dev) return efail(RS_ERR_ARG, "rs_copy_status: NULL workspace");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  uint32_t v = 0;
+  cudaError_t e = cudaMemcpyAsync(&v, static_cast<const char*>(workspace_dev) + status_offset(info->n_entries), sizeof(v),
+                                  cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return cuda_fail(e, "rs_copy_status: reading the status block");
+  *status = v;
   return RS_OK;
 }
 
@@ -399,10 +683,13 @@ namespace {
 // Every GPU that loads this library holds this array (RS_NOALLOC_MAX_ENTRIES x 72 bytes, about
 // 1.2 MB) until the process exits. All calls share it.
 static __device__ __align__(256) DevSeg g_noalloc_table[RS_NOALLOC_MAX_ENTRIES];
+// Status word of the last no-allocation launch (same bits as the workspace status block).
+static __device__ uint32_t g_noalloc_status;
 
 constexpr int kMaxDevices = 64;
 // Device address of g_noalloc_table per device ordinal, set once by the first call on that device.
 DevSeg* g_noalloc_addr[kMaxDevices] = {nullptr};
+uint32_t* g_noalloc_status_addr[kMaxDevices] = {nullptr};
 std::mutex g_noalloc_mu;
 
 int noalloc_table_addr(int dev, DevSeg** out) {
@@ -412,9 +699,13 @@ int noalloc_table_addr(int dev, DevSeg** out) {
     // In host code the array's name is only a stand-in; the device address has to be looked up,
     // with the device current.
     void* p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_table);
+    void* q = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_table);
+    if (e != cudaSuccess) return cuda_fail(e, "rs_copy_launch_noalloc: cudaGetSymbolAddress");
+    e = cudaGetSymbolAddress(&q, g_noalloc_status);
     if (e != cudaSuccess) return cuda_fail(e, "rs_copy_launch_noalloc: cudaGetSymbolAddress");
     g_noalloc_addr[dev] = static_cast<DevSeg*>(p);
+    g_noalloc_status_addr[dev] = static_cast<uint32_t*>(q);
   }
   *out = g_noalloc_addr[dev];
   return RS_OK;
@@ -452,56 +743,42 @@ int rs_copy_launch_noalloc(const rs_copy_desc* descs, int64_t n_desc, void* stre
   int nc = 0;
   int64_t written = 0;
   uint64_t ntiles = 0, total = 0;
-  for (int64_t i = 0; i < n_desc; ++i) {
-    const rs_copy_desc& d = descs[i];
-    if (d.rows == 0 || d.row_bytes == 0) continue;
-    if (d.rows > 0xffffffffull) return efail(RS_ERR_ARG, "rs_copy_launch_noalloc: entry " + std::to_string(i) + " has more than 2^32 rows");
-    if (d.rows > 1 && (d.row_bytes > d.src_pitch || d.row_bytes > d.dst_pitch))
-      return efail(RS_ERR_ARG, "rs_copy_launch_noalloc: entry " + std::to_string(i) + " has rows longer than their pitch");
-    if (!d.src_dev || !d.dst_dev) return efail(RS_ERR_ARG, "rs_copy_launch_noalloc: entry " + std::to_string(i) + " has a NULL address");
-    DevSeg& s = chunk[nc++];
-    s.src = d.src_dev;
-    s.dst = d.dst_dev;
-    s.src_pitch = d.src_pitch;
-    s.dst_pitch = d.dst_pitch;
-    s.rows = (uint32_t)d.rows;
-    s.row_bytes = d.row_bytes;
-    s.vshift = vector_shift(d);
-    s.tile_begin = ntiles;
-    if (d.row_bytes >= tile_bytes) {
-      s.col_bytes = tile_bytes;
-      s.col_tiles = (uint32_t)((d.row_bytes + tile_bytes - 1) / tile_bytes);
-      s.rows_per_tile = 1;
-      ntiles += (uint64_t)s.col_tiles * d.rows;
-    } else {
-      s.col_bytes = d.row_bytes;
-      s.col_tiles = 1;
-      const uint64_t pitch = std::max(d.src_pitch, d.dst_pitch);
-      const uint64_t rows_32 = pitch ? (0xffffffffull - d.row_bytes) / pitch + 1 : 1;
-      s.rows_per_tile = (uint32_t)std::max<uint64_t>(1, std::min<uint64_t>(tile_bytes / d.row_bytes, rows_32));
-      ntiles += (d.rows + s.rows_per_tile - 1) / s.rows_per_tile;
+  uint64_t nremote = 0;
+  for (int pass = 0; pass < 2; ++pass) {  // remote entries first, then local ones
+    for (int64_t i = 0; i < n_desc; ++i) {
+      const rs_copy_desc& d = descs[i];
+      if (empty_desc(d) || remote_desc(d) != (pass == 0)) continue;
+      rc = make_entry(d, i, tile_bytes, ntiles, chunk[nc++], "rs_copy_launch_noalloc");
+      if (rc) return rc;
+      total += d.rows * d.row_bytes;
+      if (nc == kChunk || written + nc == n_entries) {
+        e = cudaMemcpyAsync(table + written, chunk, nc * sizeof(DevSeg), cudaMemcpyHostToDevice, st);
+        if (e != cudaSuccess) return cuda_fail(e, "rs_copy_launch_noalloc: staging the copy table");
+        written += nc;
+        nc = 0;
+      }
     }
-    total += d.rows * d.row_bytes;
-    if (nc == kChunk || written + nc == n_entries) {
-      e = cudaMemcpyAsync(table + written, chunk, nc * sizeof(DevSeg), cudaMemcpyHostToDevice, st);
-      if (e != cudaSuccess) return cuda_fail(e, "rs_copy_launch_noalloc: staging the copy table");
-      written += nc;
-      nc = 0;
-    }
+    if (pass == 0) nremote = ntiles;
   }
   int sms = 0, per_sm = 0;
   const Variant& v = kVariants[variant];
+  uint32_t* status = g_noalloc_status_addr[dev];
+  if ((e = cudaMemsetAsync(status, 0, sizeof(uint32_t), st)) != cudaSuccess) return cuda_fail(e, "rs_copy_launch_noalloc: clearing status");
   if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
-  if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, v.fn, v.block, 0)) != cudaSuccess)
+  if (v.smem > 0 &&
+      (e = cudaFuncSetAttribute(v.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)v.smem)) != cudaSuccess)
+    return cuda_fail(e, "rs_copy_launch_noalloc: cudaFuncSetAttribute");
+  if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, v.fn, v.block, v.smem)) != cudaSuccess)
     return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
   per_sm = (int)std::min<uint64_t>((uint64_t)std::max(per_sm, 1), env_u64("SUIKA_RS_CTAS_PER_SM", 8));
   li->n_entries = n_entries;
   li->n_tiles = ntiles;
+  li->n_tiles_remote = nremote;
   li->total_bytes = total;
   li->variant = variant;
   li->grid = (int32_t)std::min<uint64_t>(ntiles, (uint64_t)sms * (uint64_t)per_sm);
   li->block = v.block;
-  v.fn<<<(unsigned)li->grid, v.block, 0, st>>>(table, (int32_t)n_entries, ntiles);
+  v.fn<<<(unsigned)li->grid, v.block, v.smem, st>>>(table, (int32_t)n_entries, ntiles, nremote, status);
   if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(e, "rs_copy_launch_noalloc: kernel launch");
   return RS_OK;
 }

@@ -364,6 +364,7 @@ int rs_version(int32_t* major, int32_t* minor) {
 // target is `rank`).
 // ---------------------------------------------------------------------------------------------
 struct rs_program {
+  int32_t rank = -1;
   std::vector<rs_dst_slot> dst;
   std::vector<rs_src_slot> src;
   std::vector<rs_meta_slot> meta;
@@ -518,6 +519,7 @@ int rs_program_build(const rs_plan* plan, int32_t rank, const rs_subfield* subfi
     if (subfields[f].itemsize <= 0) return fail(RS_ERR_SUBFIELD, "rs_program_build: sub-field itemsize must be positive");
   rs_program* prog = new (std::nothrow) rs_program();
   if (!prog) return fail(RS_ERR_ARG, "rs_program_build: out of host memory");
+  prog->rank = rank;
   try {
     if (plan->mode == 1) {
       int rc = program_from_pieces(plan, rank, subfields, n_subfields, prog);
@@ -721,6 +723,10 @@ int resolve_segments(const rs_program* prog, int32_t src_rank, const uint64_t* s
     c.row_bytes = s.row_bytes;
     c.src_pitch = s.src_pitch;
     c.dst_pitch = s.dst_pitch;
+    // remote: the copying rank (the source rank when filtered by it) is not the other end
+    const int32_t copier = src_rank >= 0 ? src_rank : prog->rank;
+    const int32_t other = src_rank >= 0 ? prog->rank : prog->src[s.src_slot].src_rank;
+    c.flags = copier != other ? RS_COPY_REMOTE : 0u;
   }
   if (n_out) *n_out = k;
   return RS_OK;
@@ -763,6 +769,7 @@ int rs_program_resolve(const rs_program* prog, const uint64_t* src_dev, const ui
     c.row_bytes = s.row_bytes;
     c.src_pitch = s.src_pitch;
     c.dst_pitch = s.dst_pitch;
+    c.flags = prog->src[s.src_slot].src_rank != prog->rank ? RS_COPY_REMOTE : 0u;
   }
   return RS_OK;
 }

@@ -377,6 +377,18 @@ class PreparedCopies:
         L.check(self._lib.rs_copy_run(self.workspace.data_ptr(), C.byref(self.info), C.c_void_p(stream.cuda_stream)))
         return self.info
 
+    def status(self, stream: Optional[torch.cuda.Stream] = None) -> int:
+        """Status bits of the launches so far (synchronises the stream); 0 means no error."""
+        stream = stream or torch.cuda.current_stream(self.device)
+        v = C.c_uint32()
+        L.check(self._lib.rs_copy_status(self.workspace.data_ptr(), C.byref(self.info), C.c_void_p(stream.cuda_stream), C.byref(v)))
+        return int(v.value)
+
+    def check(self, stream: Optional[torch.cuda.Stream] = None) -> None:
+        st = self.status(stream)
+        if st:
+            raise L.ReshardError(L.RS_ERR_CUDA, f"copy kernel reported status {st:#x} (a bounded wait ran out; targets incomplete)")
+
 
 def launch_copies(descs: np.ndarray, device: torch.device, stream: Optional[torch.cuda.Stream] = None) -> L.RsLaunchInfo:
     """Stage a COPY_DESC table and run it with one sm_100a kernel launch on `stream` (asynchronous).
@@ -478,7 +490,7 @@ class _MetaStage:
         d = np.zeros(len(self.targets), dtype=L.COPY_DESC_DTYPE)
         base = stage.data_ptr()
         for i, (o, s, t) in enumerate(zip(offs, sizes, self.targets)):
-            d[i] = (base + int(o), t.data_ptr(), 1, s, s, s)
+            d[i] = (base + int(o), t.data_ptr(), 1, s, s, s, 0)
         return d, stage
 
 
@@ -618,7 +630,56 @@ def _export(tensors: List[torch.Tensor]):
     return handles, where
 
 
-class RankTransfer:
+def plan_phases(plan: "Plan", phased: bool = True) -> Tuple[Dict[Tuple[int, int], int], int]:
+    """Phase of every remote (source, target) pair of a plan (transfer_phases), and the count."""
+    if not phased:
+        return {}, 1
+    ops = plan.op_array
+    m = ops["src_rank"] != ops["dst_rank"]
+    pairs: Dict[Tuple[int, int], int] = {}
+    for s, t, n in zip(ops["src_rank"][m], ops["dst_rank"][m], ops["numel"][m]):
+        pairs[(int(s), int(t))] = pairs.get((int(s), int(t)), 0) + int(n)
+    col = transfer_phases(pairs)
+    return col, (max(col.values()) + 1) if col else 1
+
+
+class _Phased:
+    """Per-phase staged tables of one rank, run with a barrier between phases."""
+
+    def _stage_phases(self, table: np.ndarray, peer_of_entry: np.ndarray, as_source: bool, phased: bool):
+        self.phase_of_pair, self.n_phases = plan_phases(self.plan, phased)
+        tables = _phase_tables(table, peer_of_entry, self.rank, self.phase_of_pair, self.n_phases, as_source)
+        self.prepared_phases = [PreparedCopies(t, self.device) if len(t) else None for t in tables]
+        self.prepared = self.prepared_phases[0] if self.n_phases == 1 else None
+
+    def launch(self, stream: Optional[torch.cuda.Stream] = None) -> L.RsLaunchInfo:
+        """Queue every phase of this rank back to back (asynchronous); no cross-rank pacing."""
+        info = L.RsLaunchInfo()
+        for p in getattr(self, "prepared_phases", []):
+            if p is not None:
+                info = p.launch(stream)
+        return info
+
+    def run(self) -> None:
+        """Run the phases in step with the other ranks: phase k+1 starts on every rank after every
+        rank has finished phase k (host barrier), so each GPU talks to one peer per direction."""
+        phases = getattr(self, "prepared_phases", [])
+        for k in range(getattr(self, "n_phases", 1)):
+            if k:
+                torch.cuda.current_stream(self.device).synchronize()
+                dist.barrier(group=self.world)
+            if k < len(phases) and phases[k] is not None:
+                phases[k].launch()
+
+    def _status(self) -> int:
+        st = 0
+        for p in getattr(self, "prepared_phases", []):
+            if p is not None:
+                st |= p.status()
+        return st
+
+
+class RankTransfer(_Phased):
     """One rank's share of a reshard, split into prepare / launch / finish so that the data path
     (launch) can be run and timed on its own.
 
@@ -633,7 +694,8 @@ class RankTransfer:
     """
 
     def __init__(self, plan: Plan, source_state_dict: Dict[str, Dict[str, torch.Tensor]], expected_sub_fields,
-                 device: torch.device, world: Optional[dist.ProcessGroup] = None, log_func: Optional[Callable] = None):
+                 device: torch.device, world: Optional[dist.ProcessGroup] = None, log_func: Optional[Callable] = None,
+                 phased: bool = True):
         self.plan, self.device, self.world = plan, device, world
         self.source_state_dict = source_state_dict
         self.log = log_func or (lambda m: None)
@@ -681,6 +743,7 @@ class RankTransfer:
         self.remote_bytes = self.local_bytes = 0
         self._stage = None
         self.prepared = None
+        self.prepared_phases, self.n_phases = [], plan_phases(plan, phased)[1]
         self.peers = _PeerMaps()
         if not np.any(ops["dst_rank"] == rank):
             return
@@ -725,7 +788,9 @@ class RankTransfer:
                 ent.setdefault(name, {})[s] = x
             md, self._stage = meta.descs()
             self.table = np.concatenate([table, md])
-            self.prepared = PreparedCopies(self.table, device)
+            peer = np.concatenate([prog.src_slots["src_rank"][prog.segments["src_slot"]].astype(np.int64),
+                                   np.full(len(md), rank, np.int64)])
+            self._stage_phases(self.table, peer, as_source=False, phased=phased)
             self.remote_bytes, self.local_bytes = prog.remote_bytes, prog.local_bytes
             self.target = {plan.names[n]: {s: ent[plan.names[n]][s] for s in subs if s in ent[plan.names[n]]}
                            for n in _name_order(plan, rank)}
@@ -733,21 +798,19 @@ class RankTransfer:
             self.peers.close()
             raise
 
-    def launch(self, stream: Optional[torch.cuda.Stream] = None) -> L.RsLaunchInfo:
-        """Queue this rank's pulls (asynchronous; one kernel launch over the staged table)."""
-        if self.prepared is None:
-            return L.RsLaunchInfo()
-        return self.prepared.launch(stream)
-
     def finish(self) -> Dict[str, Dict[str, torch.Tensor]]:
         """Wait for this rank's kernel, then for every rank (barrier); release peers and sources."""
         try:
             torch.cuda.current_stream(self.device).synchronize()
+            st = self._status()
             dist.barrier(group=self.world)  # every reader of this rank's sources has finished
         finally:
             self.peers.close()
+        if st:
+            raise L.ReshardError(L.RS_ERR_CUDA, f"rank {self.rank}: copy kernel reported status {st:#x}; targets incomplete")
         self._stage = None
         self.prepared = None
+        self.prepared_phases = []
         self.source_state_dict.clear()
         self.log(f"suika_b200: rank {self.rank} pulled {self.remote_bytes} B from peers and {self.local_bytes} B "
                  f"locally with {len(self.table)} copies")
@@ -781,7 +844,7 @@ def _push_table(prog: Program, rank: int, src_addr: Callable[[str, str], Tuple[i
     return out[: n.value]
 
 
-class RankTransferPush:
+class RankTransferPush(_Phased):
     """One rank's share of a reshard with targets written by their sources (same contract as
     RankTransfer: prepare / launch / finish, same targets byte for byte).
 
@@ -797,7 +860,8 @@ class RankTransferPush:
     """
 
     def __init__(self, plan: Plan, source_state_dict: Dict[str, Dict[str, torch.Tensor]], expected_sub_fields,
-                 device: torch.device, world: Optional[dist.ProcessGroup] = None, log_func: Optional[Callable] = None):
+                 device: torch.device, world: Optional[dist.ProcessGroup] = None, log_func: Optional[Callable] = None,
+                 phased: bool = True):
         self.plan, self.device, self.world = plan, device, world
         self.source_state_dict = source_state_dict
         self.log = log_func or (lambda m: None)
@@ -831,6 +895,7 @@ class RankTransferPush:
         self.target: Dict[str, Dict[str, torch.Tensor]] = {}
         self.remote_bytes = self.local_bytes = 0
         self.prepared = None
+        self.prepared_phases, self.n_phases = [], plan_phases(plan, phased)[1]
         self._stage = None
         my_prog = plan.program(rank, spec) if np.any(ops["dst_rank"] == rank) else None
         arena_handle, arena_offset, slot_off, slot_nb = None, 0, np.zeros(0, np.uint64), np.zeros(0, np.uint64)
@@ -850,7 +915,7 @@ class RankTransferPush:
                                group=world)
         try:
             # 3. the pieces this rank sources, for every target rank
-            tables = []
+            tables, peers_of = [], []
             targets = sorted(set(int(t) for t in ops["dst_rank"][ops["src_rank"] == rank]))
             def src_addr(name, sub):
                 if name not in source_state_dict:
@@ -869,6 +934,7 @@ class RankTransferPush:
                 else:
                     self.remote_bytes += nbytes
                 tables.append(d)
+                peers_of.append(np.full(len(d), T, np.int64))
             # 4. this rank's targets: dict in the reference's order, singleton values staged locally
             if my_prog is not None:
                 ent: Dict[str, Dict[str, torch.Tensor]] = {}
@@ -888,30 +954,29 @@ class RankTransferPush:
                     ent.setdefault(name, {})[s] = x
                 md, self._stage = meta.descs()
                 tables.append(md)
+                peers_of.append(np.full(len(md), rank, np.int64))
                 self.target = {plan.names[n]: {s: ent[plan.names[n]][s] for s in subs if s in ent[plan.names[n]]}
                                for n in _name_order(plan, rank)}
             self.table = np.concatenate(tables) if tables else np.zeros(0, dtype=L.COPY_DESC_DTYPE)
-            if len(self.table):
-                self.prepared = PreparedCopies(self.table, device)
+            peer = np.concatenate(peers_of) if peers_of else np.zeros(0, np.int64)
+            self._stage_phases(self.table, peer, as_source=True, phased=phased)
         except BaseException:
             self.peers.close()
             raise
-
-    def launch(self, stream: Optional[torch.cuda.Stream] = None) -> L.RsLaunchInfo:
-        """Queue this rank's writes (asynchronous; one kernel launch over the staged table)."""
-        if self.prepared is None:
-            return L.RsLaunchInfo()
-        return self.prepared.launch(stream)
 
     def finish(self) -> Dict[str, Dict[str, torch.Tensor]]:
         """Wait for this rank's kernel, then for every rank (barrier): all pieces have landed."""
         try:
             torch.cuda.current_stream(self.device).synchronize()
+            st = self._status()
             dist.barrier(group=self.world)
         finally:
             self.peers.close()
+        if st:
+            raise L.ReshardError(L.RS_ERR_CUDA, f"rank {self.rank}: copy kernel reported status {st:#x}; targets incomplete")
         self._stage = None
         self.prepared = None
+        self.prepared_phases = []
         self.source_state_dict.clear()
         self.log(f"suika_b200: rank {self.rank} wrote {self.remote_bytes} B to peers and {self.local_bytes} B locally")
         return self.target
@@ -919,20 +984,21 @@ class RankTransferPush:
 
 def execute_plan_distributed(plan: Plan, source_state_dict: Dict[str, Dict[str, torch.Tensor]], expected_sub_fields,
                              device: torch.device, world: Optional[dist.ProcessGroup] = None,
-                             log_func: Optional[Callable] = None, timers: Optional[dict] = None, direction: str = "pull"):
+                             log_func: Optional[Callable] = None, timers: Optional[dict] = None, direction: str = "pull",
+                             phased: bool = True):
     """Run one rank's share of a reshard (execute_param_transfer, migration.py:397-556): prepare,
     one kernel launch, finish. Collective over `world`. direction="pull": each target rank reads
     its pieces (RankTransfer); "push": each source rank writes them (RankTransferPush)."""
     cls = {"pull": RankTransfer, "push": RankTransferPush}[direction]
-    rt = cls(plan, source_state_dict, expected_sub_fields, device, world, log_func)
+    rt = cls(plan, source_state_dict, expected_sub_fields, device, world, log_func, phased=phased)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record()
-    info = rt.launch()
+    rt.run()
     ev1.record()
     target = rt.finish()
     if timers is not None:
         timers["kernel_ms"] = ev0.elapsed_time(ev1)
-        timers["n_tiles"], timers["total_bytes"] = int(info.n_tiles), int(info.total_bytes)
+        timers["phases"] = rt.n_phases
         timers["remote_bytes"], timers["local_bytes"] = rt.remote_bytes, rt.local_bytes
     return target
 
@@ -946,6 +1012,11 @@ def schedule_and_execute_param_transfer(source_param_layout, target_param_layout
     contiguous), same side effect (source_state_dict cleared). The targets are byte-identical to
     the reference's, including its order of concatenated pieces. `forcefully_free` is accepted for
     signature compatibility: no temporary piece tensors exist to free.
+
+    direction (default: $SUIKA_RESHARD_DIRECTION, else "push"): "push" has every source rank write
+    its pieces into the target ranks' memory (targets of a rank are views of one arena); "pull" has
+    every target rank read them (targets are separate allocations). Transfers run in phases in
+    which every GPU sends to at most one peer and receives from at most one.
     """
     if not isinstance(device, torch.device):
         device = torch.device(device)
@@ -956,7 +1027,7 @@ def schedule_and_execute_param_transfer(source_param_layout, target_param_layout
     plan = Plan(source_param_layout, target_param_layout)
     prof.stop("schedule")
     prof.start("execute", require_memory=True)
-    direction = direction or os.environ.get("SUIKA_RESHARD_DIRECTION", "pull")
+    direction = direction or os.environ.get("SUIKA_RESHARD_DIRECTION", "push")
     target = execute_plan_distributed(plan, source_state_dict, other_context_dict["expected_sub_fields"], device, world, log_func,
                                       direction=direction)
     torch.cuda.synchronize(device=device)
@@ -994,3 +1065,67 @@ def execute_param_transfer(transfer_ops: TransferSchedule, source_state_dict, de
     if device.type != "cuda":
         raise RuntimeError("suika_b200 moves state on CUDA devices only (no CPU path)")
     return execute_plan_distributed(transfer_ops.plan, source_state_dict, expected_sub_fields, device, world, log_func)
+
+
+# ---------------------------------------------------------------------------------------------
+# Transfer phases: at most one peer per direction per GPU at a time.
+# ---------------------------------------------------------------------------------------------
+def transfer_phases(pairs: Dict[Tuple[int, int], int]) -> Dict[Tuple[int, int], int]:
+    """Phase of every remote (source, target) rank pair such that within a phase every rank sends
+    to at most one peer and receives from at most one: a proper edge colouring of the bipartite
+    source -> target multigraph with as many colours as its largest degree (Konig), found by
+    alternating-path recolouring. Heavier pairs are coloured first. pairs: {(s, t): bytes}, s != t."""
+    color: Dict[Tuple[int, int], int] = {}
+    at_src: Dict[int, Dict[int, int]] = {}   # s -> {colour: t}
+    at_dst: Dict[int, Dict[int, int]] = {}   # t -> {colour: s}
+    deg: Dict[Tuple[str, int], int] = {}
+    for s, t in pairs:
+        deg[("s", s)] = deg.get(("s", s), 0) + 1
+        deg[("t", t)] = deg.get(("t", t), 0) + 1
+    ncol = max(deg.values(), default=0)
+    for (s, t) in sorted(pairs, key=lambda p: (-pairs[p], p)):
+        cs, ct = at_src.setdefault(s, {}), at_dst.setdefault(t, {})
+        a = next(c for c in range(ncol) if c not in cs)   # free at the source
+        b = next(c for c in range(ncol) if c not in ct)   # free at the target
+        if a != b and a in ct:
+            # flip the a/b alternating path that starts at target t along colour a
+            path, node, side, c = [], t, "t", a
+            while True:
+                nxt = (at_dst if side == "t" else at_src).get(node, {}).get(c)
+                if nxt is None:
+                    break
+                e = (nxt, node) if side == "t" else (node, nxt)
+                path.append(e)
+                node, side, c = nxt, ("s" if side == "t" else "t"), (b if c == a else a)
+            for e in path:  # remove, then re-add with swapped colours
+                old = color[e]
+                del at_src[e[0]][old], at_dst[e[1]][old]
+            for e in path:
+                new = b if color[e] == a else a
+                color[e] = new
+                at_src[e[0]][new], at_dst[e[1]][new] = e[1], e[0]
+        color[(s, t)] = a
+        cs[a], ct[a] = t, s
+    return color
+
+
+def _phase_tables(table: np.ndarray, peer_of_entry: np.ndarray, rank: int, phase_of_pair, n_phases: int,
+                  as_source: bool) -> List[np.ndarray]:
+    """Split a rank's table by phase: a remote entry goes to the phase of its (source, target)
+    pair; local entries are spread over the phases, each to the one with the fewest bytes so far."""
+    if n_phases <= 1:
+        return [table]
+    nbytes = (table["rows"] * table["row_bytes"]).astype(np.int64)
+    phase = np.zeros(len(table), np.int64)
+    load = np.zeros(n_phases, np.int64)
+    remote = peer_of_entry != rank
+    for i in np.nonzero(remote)[0]:
+        p = int(peer_of_entry[i])
+        k = phase_of_pair[(rank, p) if as_source else (p, rank)]
+        phase[i] = k
+        load[k] += nbytes[i]
+    for i in np.nonzero(~remote)[0]:
+        k = int(np.argmin(load))
+        phase[i] = k
+        load[k] += nbytes[i]
+    return [table[phase == k] for k in range(n_phases)]

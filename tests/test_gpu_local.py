@@ -90,12 +90,14 @@ def test_views_move_only_row_split_pieces():
     assert info.total_bytes == moved + 4 * len([1 for r in (0, 1) for _ in out[r]])  # + one 4-byte step per tensor
 
 
+@pytest.mark.parametrize("variant", ["1", "2", "3", "4", "5", "6", "7"])
 @pytest.mark.parametrize("tile", ["256", "4096", "131072"])
-def test_copy_kernel_random_rectangles(tile, monkeypatch):
-    """Strided copies with random alignment, pitch and size (every vector width, column-split rows)
-    against torch's own copy of the same rectangles."""
+def test_copy_kernel_random_rectangles(tile, variant, monkeypatch):
+    """Strided copies with random alignment, pitch and size (every vector width, column-split rows),
+    for every launch shape (vector copies and TMA bulk copies), against torch's own copy."""
     monkeypatch.setenv("SUIKA_RS_TILE_BYTES", tile)
-    rng = np.random.default_rng(int(tile))
+    monkeypatch.setenv("SUIKA_RS_VARIANT", variant)
+    rng = np.random.default_rng(int(tile) + int(variant))
     src = torch.randint(0, 255, (8 << 20,), dtype=torch.uint8, device=DEV)
     dst = torch.zeros(16 << 20, dtype=torch.uint8, device=DEV)
     want = torch.zeros_like(dst)
@@ -111,13 +113,16 @@ def test_copy_kernel_random_rectangles(tile, monkeypatch):
         dpos += int(rng.integers(0, 17))
         if dpos + rows * dp >= dst.numel():
             break
-        descs.append((src.data_ptr() + so, dst.data_ptr() + dpos, rows, rb, sp, dp))
+        descs.append((src.data_ptr() + so, dst.data_ptr() + dpos, rows, rb, sp, dp, int(rng.integers(0, 2))))
         for r in range(rows):
             want[dpos + r * dp: dpos + r * dp + rb] = src[so + r * sp: so + r * sp + rb]
         dpos += rows * dp
     table = np.array(descs, dtype=M.L.COPY_DESC_DTYPE)
-    M.launch_copies(table, DEV)
+    prepared = M.PreparedCopies(table, DEV)
+    info = prepared.launch()
+    assert info.variant == int(variant) - 1
     torch.cuda.synchronize()
+    assert prepared.status() == 0
     assert torch.equal(dst, want)
 
 

@@ -151,3 +151,20 @@ def test_resolve_rejects_out_of_bounds():
     from suika_b200._lib import ReshardError
     with pytest.raises(ReshardError, match="leaves"):
         prog.resolve(np.full(n, 4096, np.uint64), np.full(n, 63, np.uint64), np.full(1, 8192, np.uint64), np.full(1, 32, np.uint64))
+
+
+def test_resolve_marks_remote_pieces():
+    """Entries whose source is another rank carry RS_COPY_REMOTE; the executor stages them first
+    and interleaves them with local entries in every CTA."""
+    cfg = CASES["cfg3_mini"]["config"]
+    spl, tpl = cfg.layouts()
+    plan = M.Plan(spl, tpl, minimum_est_peers=1)
+    for rank in range(8):
+        prog = plan.program(rank, SUBFIELD_SPEC)
+        n = len(prog.src_slots)
+        m = len(prog.dst_slots)
+        out = prog.resolve(np.full(n, 1 << 40, np.uint64), np.full(n, 1 << 40, np.uint64),
+                           np.full(m, 1 << 41, np.uint64), np.full(m, 1 << 40, np.uint64))
+        want = (prog.src_slots["src_rank"][prog.segments["src_slot"]] != rank).astype(np.uint64)
+        assert np.array_equal(out["flags"], want)
+        assert want.any()

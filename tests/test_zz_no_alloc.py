@@ -42,8 +42,10 @@ def _run_both(descs_rel, dst_a, dst_b):
     """Same copies into dst_a with rs_copy_launch and into dst_b with rs_copy_launch_noalloc."""
     lib = L.load()
     stream = C.c_void_p(torch.cuda.current_stream(DEV).cuda_stream)
-    ta = np.array([(s, dst_a.data_ptr() + o, r, rb, sp, dp) for s, o, r, rb, sp, dp in descs_rel], dtype=L.COPY_DESC_DTYPE)
-    tb = np.array([(s, dst_b.data_ptr() + o, r, rb, sp, dp) for s, o, r, rb, sp, dp in descs_rel], dtype=L.COPY_DESC_DTYPE)
+    ta = np.array([(s, dst_a.data_ptr() + o, r, rb, sp, dp, k % 2) for k, (s, o, r, rb, sp, dp) in enumerate(descs_rel)],
+                  dtype=L.COPY_DESC_DTYPE)
+    tb = np.array([(s, dst_b.data_ptr() + o, r, rb, sp, dp, k % 2) for k, (s, o, r, rb, sp, dp) in enumerate(descs_rel)],
+                  dtype=L.COPY_DESC_DTYPE)
     M.launch_copies(ta, DEV)
     info = L.RsLaunchInfo()
     L.check(lib.rs_copy_launch_noalloc(tb.ctypes.data, len(tb), stream, C.byref(info)))
