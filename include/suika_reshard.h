@@ -302,6 +302,10 @@ int rs_copy_launch(const rs_copy_desc* descs, int64_t n_desc,
 #define RS_NOALLOC_MAX_ENTRIES 16384
 int rs_copy_launch_noalloc(const rs_copy_desc* descs, int64_t n_desc, void* stream, rs_launch_info* info);
 
+/* Device address of page-locked host memory (cudaHostAlloc / cudaHostRegister), for copy tables
+ * that read host memory directly over PCIe (checkpoint resume, migration.py:1235-1244). */
+int rs_host_device_pointer(const void* host_ptr, void** dev_ptr);
+
 /* ---- peer memory (replaces NCCL P2P connections, utils.py:212-236) ----------------------- */
 typedef struct rs_peer_handle {
   uint8_t ipc[64];          /* cudaIpcMemHandle_t of the allocation      */

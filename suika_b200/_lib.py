@@ -150,6 +150,7 @@ SIGNATURES = {
     "rs_copy_status": (C.c_int, [_P, C.POINTER(RsLaunchInfo), _P, C.POINTER(C.c_uint32)]),
     "rs_copy_launch": (C.c_int, [_P, C.c_int64, _P, C.c_uint64, _P, C.POINTER(RsLaunchInfo)]),
     "rs_copy_launch_noalloc": (C.c_int, [_P, C.c_int64, _P, C.POINTER(RsLaunchInfo)]),
+    "rs_host_device_pointer": (C.c_int, [_P, C.POINTER(_P)]),
     "rs_peer_export": (C.c_int, [_P, C.POINTER(RsPeerHandle), C.POINTER(C.c_uint64)]),
     "rs_peer_open": (C.c_int, [C.POINTER(RsPeerHandle), C.POINTER(_P)]),
     "rs_peer_close": (C.c_int, [_P]),

@@ -627,6 +627,14 @@ int address_range(const void* ptr, uint64_t* base, uint64_t* bytes) {
 
 extern "C" {
 
+int rs_host_device_pointer(const void* host_ptr, void** dev_ptr) {
+  if (!host_ptr || !dev_ptr) return efail(RS_ERR_ARG, "rs_host_device_pointer: NULL argument");
+  *dev_ptr = nullptr;
+  cudaError_t e = cudaHostGetDevicePointer(dev_ptr, const_cast<void*>(host_ptr), 0);
+  if (e != cudaSuccess) return cuda_fail(e, "rs_host_device_pointer: cudaHostGetDevicePointer (memory must be page-locked)");
+  return RS_OK;
+}
+
 int rs_peer_export(const void* ptr_dev, rs_peer_handle* out, uint64_t* offset) {
   if (!ptr_dev || !out || !offset) return efail(RS_ERR_ARG, "rs_peer_export: NULL argument");
   std::memset(out, 0, sizeof(*out));

@@ -1028,9 +1028,16 @@ def schedule_and_execute_param_transfer(source_param_layout, target_param_layout
     prof.stop("schedule")
     prof.start("execute", require_memory=True)
     direction = direction or os.environ.get("SUIKA_RESHARD_DIRECTION", "push")
+    release = getattr(source_state_dict, "release", None)
+    if callable(release):
+        # sources received in place from the old process (suika_b200.handoff) are memory another
+        # process owns: they cannot be re-exported to peers, so this rank's own kernel reads them
+        direction = "push"
     target = execute_plan_distributed(plan, source_state_dict, other_context_dict["expected_sub_fields"], device, world, log_func,
                                       direction=direction)
     torch.cuda.synchronize(device=device)
+    if callable(release):
+        release()  # every rank is past the barrier: the old process may free its memory
     prof.stop("execute", require_memory=True)
     return target
 
@@ -1054,17 +1061,88 @@ def schedule_param_transfer(source_param_layout, target_param_layout, log_func: 
 
 
 def execute_param_transfer(transfer_ops: TransferSchedule, source_state_dict, device, expected_sub_fields, world=None,
-                           log_func=None, prof=None, forcefully_free: bool = False, fake_source_state_dicts=None):
+                           log_func=None, prof=None, forcefully_free: bool = False, fake_source_state_dicts=None,
+                           rank: Optional[int] = None):
     """Drop-in for execute_param_transfer (migration.py:397-556) on a schedule made by
-    schedule_param_transfer above (the C plan travels with it)."""
+    schedule_param_transfer above (the C plan travels with it).
+
+    With fake_source_state_dicts (checkpoint resume, migration.py:1235-1244: every needed source
+    shard loaded from disk into host memory) the targets are built on `device` (CUDA) straight from
+    host memory: the needed source tensors are gathered into one page-locked arena and the copy
+    kernel reads them over PCIe. No collective is used; `rank` overrides dist.get_rank(world)."""
     if not isinstance(transfer_ops, TransferSchedule):
         raise TypeError("execute_param_transfer needs the schedule returned by suika_b200's schedule_param_transfer")
-    if fake_source_state_dicts is not None:
-        raise NotImplementedError("the checkpoint-resume path (fake_source_state_dicts) is not built yet")
     device = torch.device(device)
     if device.type != "cuda":
         raise RuntimeError("suika_b200 moves state on CUDA devices only (no CPU path)")
+    if fake_source_state_dicts is not None:
+        r = dist.get_rank(world) if rank is None else rank
+        return execute_from_host(transfer_ops.plan, r, source_state_dict, fake_source_state_dicts, expected_sub_fields, device)
     return execute_plan_distributed(transfer_ops.plan, source_state_dict, expected_sub_fields, device, world, log_func)
+
+
+def execute_from_host(plan: Plan, rank: int, source_state_dict, fake_source_state_dicts, expected_sub_fields,
+                      device: torch.device) -> Dict[str, Dict[str, torch.Tensor]]:
+    """Checkpoint resume on B200: this rank's targets from host-resident source shards.
+
+    Same bytes and cat order as the reference's checkpoint path; like it, every target takes its
+    source's dtype, and a singleton target keeps its source's shape (recv_tensor =
+    tensor_from_fake_source.to(device), migration.py:477-482)."""
+    subs = [s for s, _ in expected_sub_fields]
+    srcs = dict(fake_source_state_dicts)
+    if source_state_dict:
+        srcs.setdefault(rank, source_state_dict)
+    dtypes = _sub_dtypes(expected_sub_fields, srcs.values())
+    spec = _program_spec(expected_sub_fields, dtypes)
+    if not np.any(plan.op_array["dst_rank"] == rank):
+        return {}
+    prog = plan.program(rank, spec)
+
+    def host_src(sr, name, sub):
+        st = srcs.get(sr)
+        if st is None or name not in st:
+            raise AssertionError(f"[{rank}]: param missing in source {name} of rank {sr}")
+        t = st[name][sub]
+        if t.device.type != "cpu":
+            raise RuntimeError(f"checkpoint source {name}[{sub}] of rank {sr} is not in host memory")
+        return t.contiguous()
+
+    # 1. the needed source slots, gathered into one page-locked arena the GPU can read directly
+    hs = [host_src(int(ss["src_rank"]), plan.names[int(ss["name_id"])], subs[int(ss["subfield"])]) for ss in prog.src_slots]
+    nb = np.array([t.numel() * t.element_size() for t in hs], np.uint64)
+    off = np.zeros(len(hs), np.uint64)
+    if len(hs) > 1:
+        off[1:] = np.cumsum((nb[:-1] + np.uint64(255)) // np.uint64(256) * np.uint64(256))
+    total = int(off[-1] + nb[-1]) if len(hs) else 0
+    arena = torch.empty(max(total, 1), dtype=torch.uint8, pin_memory=True)
+    for t, o, n in zip(hs, off, nb):
+        arena[int(o):int(o) + int(n)].copy_(t.reshape(-1).view(torch.uint8))
+    dp = C.c_void_p()
+    L.check(L.load().rs_host_device_pointer(C.c_void_p(arena.data_ptr()), C.byref(dp)))
+    # 2. targets on the device, filled by one launch reading host memory over PCIe
+    dst_t = []
+    for ds in prog.dst_slots:
+        shape = tuple(int(x) for x in ds["shape"][: ds["ndim"]])
+        dst_t.append(torch.empty(shape, dtype=dtypes[subs[ds["subfield"]]], device=device))
+    table = prog.resolve(off + np.uint64(dp.value), nb, np.array([x.data_ptr() for x in dst_t], np.uint64),
+                         np.array([x.numel() * x.element_size() for x in dst_t], np.uint64))
+    table["flags"] = L.RS_COPY_REMOTE
+    ent: Dict[str, Dict[str, torch.Tensor]] = {}
+    for ds, x in zip(prog.dst_slots, dst_t):
+        ent.setdefault(plan.names[ds["name_id"]], {})[subs[ds["subfield"]]] = x
+    meta = _MetaStage(device)
+    for ms in prog.meta_slots:
+        name, s = plan.names[int(ms["name_id"])], subs[int(ms["subfield"])]
+        v = host_src(int(ms["src_rank"]), name, s)
+        x = torch.empty(v.shape, dtype=v.dtype, device=device)
+        meta.add(v, x)
+        ent.setdefault(name, {})[s] = x
+    md, stage = meta.descs()
+    prepared = PreparedCopies(np.concatenate([table, md]), device)
+    prepared.launch()
+    prepared.check()  # synchronises: the arena and the staging buffer may go after this
+    del arena, stage
+    return {plan.names[n]: {s: ent[plan.names[n]][s] for s in subs if s in ent[plan.names[n]]} for n in _name_order(plan, rank)}
 
 
 # ---------------------------------------------------------------------------------------------
