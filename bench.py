@@ -555,6 +555,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-check", action="store_true")
     ap.add_argument("--no-phases", action="store_true", help="N > 1: run all transfers at once instead of in matching phases")
+    ap.add_argument("--handoff", action="store_true", help="time the old -> new process hand-off instead (1 GPU)")
     ap.add_argument("--direction", choices=["pull", "push"], default="push",
                     help="N > 1: target ranks read their pieces (pull) or source ranks write them (push)")
     args = ap.parse_args()
@@ -562,6 +563,9 @@ def main():
         raise SystemExit("--warmup must be >= 3")
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
+    if args.handoff:
+        print(json.dumps(run_handoff(args)), flush=True)
+        return
     if args.impl == "reference":
         if rank == 0:
             print(json.dumps(run_reference(args, max(world, args.gpus))), flush=True)
@@ -584,3 +588,90 @@ def main():
 
 if __name__ == "__main__":
     main()
+
+
+# ---------------------------------------------------------------------------------------------
+# --handoff: old -> new process hand-off of one rank's state on one GPU
+# ---------------------------------------------------------------------------------------------
+def _ref_send(queues, tensors):
+    """Suika's per-tensor protocol (Suika/utils.py:325-386): one queue message and one ack per
+    CUDA tensor, freeing each after its ack."""
+    queues[0].put(len(tensors))
+    for t in tensors:
+        queues[0].put(t, block=True)
+        queues[1].get(block=True)
+        t.untyped_storage().resize_(0)
+
+
+def _ref_recv(queues):
+    """Suika/utils.py:389-406: receive, clone, ack, one tensor at a time."""
+    n = queues[0].get(block=True)
+    out = []
+    for _ in range(n):
+        t = queues[0].get(block=True)
+        out.append(t.clone())
+        del t
+        queues[1].put(None, block=True)
+    torch.cuda.synchronize()
+    return out
+
+
+def _handoff_old(queues, mode, layers, ready):
+    from suika_b200 import handoff
+    torch.cuda.set_device(0)
+    cfg = workload(8, layers)
+    spl, _ = cfg.layouts()
+    st = {}
+    for name, m in spl.layout[1].items():  # one rank's source shard, one allocation per tensor
+        shape = S._actual_shape(m)
+        st[name] = {s: torch.empty(shape, dtype=S.TORCH_DTYPE[k], device="cuda:0").fill_(1) for s, k in S.SUBFIELDS if k != "meta"}
+        st[name]["step"] = torch.tensor(1.0)
+    torch.cuda.synchronize()
+    ready.put(sum(t.numel() * t.element_size() for e in st.values() for t in e.values() if t.is_cuda))
+    if mode == "reference":
+        _ref_send(queues, [t for e in st.values() for t in e.values() if t.is_cuda])
+    else:
+        handoff.interactive_IPC_state_dict_send(queues, {"source_param_layout": None, "source_state_dict": st, "other_context_dict": {}})
+
+
+def _handoff_new(queues, mode, result):
+    from suika_b200 import handoff
+    torch.cuda.set_device(0)
+    torch.zeros(1, device="cuda:0")
+    t0 = time.perf_counter()
+    if mode == "reference":
+        out = _ref_recv(queues)
+        n = len(out)
+    else:
+        state = handoff.interactive_IPC_state_dict_recv(queues)
+        sd = state["source_state_dict"]
+        n = sum(1 for e in sd.values() for t in e.values() if t.is_cuda)
+        torch.cuda.synchronize()
+        sd.clear()
+        sd.release()
+    result.put((time.perf_counter() - t0, n))
+
+
+def run_handoff(args):
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    res = {"metric": "old->new process hand-off of one rank's migration state (s)", "unit": "s", "higher_is_better": False,
+           "n_gpus": 1, "config": {"workload": f"one cfg3 source rank: Llama2-13B TP8 shard, {args.layers or 40} layers, "
+                                               "bf16 param + fp32 master/m/v, one allocation per tensor, old and new process on one GPU"}}
+    for mode in ("reference", "batched-zero-copy"):
+        times = []
+        for rep in range(max(1, args.steps)):
+            queues, ready, result = (ctx.Queue(), ctx.Queue()), ctx.Queue(), ctx.Queue()
+            po = ctx.Process(target=_handoff_old, args=(queues, mode, args.layers, ready))
+            po.start()
+            nbytes = ready.get()
+            pn = ctx.Process(target=_handoff_new, args=(queues, mode, result))
+            pn.start()
+            dt, n = result.get()
+            pn.join()
+            po.join()
+            times.append(dt)
+        res[mode] = {"seconds": round(statistics.median(times), 4), "tensors": n, "bytes": int(nbytes), "runs": len(times)}
+    res["value"] = res["batched-zero-copy"]["seconds"]
+    res["speedup_vs_reference_protocol"] = round(res["reference"]["seconds"] / max(res["value"], 1e-9), 1)
+    return res
