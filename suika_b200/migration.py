@@ -179,9 +179,11 @@ def _flatten_layout(layout: Dict[int, Dict[str, Any]], name_ids: Dict[str, int],
     """ParamLayout.layout -> (rank array, per-rank TENSOR_META arrays) in dict order. Slice rules
     (a `tp_rule` attribute on a meta: [(offset, size, units), ...]) are collected into `rules`."""
     ranks, arrays = [], []
+    pad = (0,) * L.RS_MAX_DIMS
+    itemsize_of: Dict[Any, int] = {}
     for rank, metas in layout.items():
-        arr = np.zeros(len(metas), dtype=L.TENSOR_META_DTYPE)
-        for i, (name, m) in enumerate(metas.items()):
+        recs = []
+        for name, m in metas.items():
             nid = name_ids.get(name)
             if nid is None:
                 nid = name_ids[name] = len(names)
@@ -191,21 +193,19 @@ def _flatten_layout(layout: Dict[int, Dict[str, Any]], name_ids: Dict[str, int],
                 rule = tuple(tuple(int(x) for x in g) for g in rule)
                 if rules.setdefault(name, rule) != rule:
                     raise ValueError(f"{name}: different slice rules in the source and target layouts")
-            shape = tuple(int(s) for s in m.shape)
+            shape = tuple(int(x) for x in m.shape)
             if len(shape) > L.RS_MAX_DIMS:
                 raise ValueError(f"{name}: more than {L.RS_MAX_DIMS} dims")
+            isz = itemsize_of.get(m.dtype)
+            if isz is None:
+                isz = itemsize_of[m.dtype] = _itemsize(m.dtype)
             tp = m.tp_meta
-            rec = arr[i]
-            rec["name_id"] = nid
-            rec["ndim"] = len(shape)
-            rec["shape"][: len(shape)] = shape
-            rec["itemsize"] = _itemsize(m.dtype)
             if tp is None:
-                rec["slice_dim"], rec["tp_index"], rec["tp_deg"] = L.RS_NO_SLICE, 0, 1
+                recs.append((nid, len(shape), shape + pad[len(shape):], isz, L.RS_NO_SLICE, 0, 1))
             else:
-                rec["slice_dim"], rec["tp_index"], rec["tp_deg"] = int(tp[0]), int(tp[1]), int(tp[2])
+                recs.append((nid, len(shape), shape + pad[len(shape):], isz, int(tp[0]), int(tp[1]), int(tp[2])))
         ranks.append(int(rank))
-        arrays.append(arr)
+        arrays.append(np.array(recs, dtype=L.TENSOR_META_DTYPE) if recs else np.zeros(0, dtype=L.TENSOR_META_DTYPE))
     return ranks, arrays
 
 
