@@ -586,9 +586,6 @@ def main():
         print(json.dumps(res), flush=True)
 
 
-if __name__ == "__main__":
-    main()
-
 
 # ---------------------------------------------------------------------------------------------
 # --handoff: old -> new process hand-off of one rank's state on one GPU
@@ -652,6 +649,22 @@ def _handoff_new(queues, mode, result):
     result.put((time.perf_counter() - t0, n))
 
 
+def _get_or_fail(q, procs, timeout_s=600.0):
+    """Queue get that gives up as soon as one of `procs` has died, or after timeout_s."""
+    import queue as _queue
+    t0 = time.perf_counter()
+    while True:
+        try:
+            return q.get(timeout=1.0)
+        except _queue.Empty:
+            dead = [p.exitcode for p in procs if not p.is_alive()]
+            if dead or time.perf_counter() - t0 > timeout_s:
+                for p in procs:
+                    if p.is_alive():
+                        p.kill()
+                raise RuntimeError(f"hand-off process failed (exit codes {[p.exitcode for p in procs]})")
+
+
 def run_handoff(args):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
@@ -664,14 +677,20 @@ def run_handoff(args):
             queues, ready, result = (ctx.Queue(), ctx.Queue()), ctx.Queue(), ctx.Queue()
             po = ctx.Process(target=_handoff_old, args=(queues, mode, args.layers, ready))
             po.start()
-            nbytes = ready.get()
+            nbytes = _get_or_fail(ready, [po])
             pn = ctx.Process(target=_handoff_new, args=(queues, mode, result))
             pn.start()
-            dt, n = result.get()
-            pn.join()
-            po.join()
+            dt, n = _get_or_fail(result, [po, pn])
+            pn.join(120)
+            po.join(120)
+            if pn.exitcode != 0 or po.exitcode != 0:
+                raise RuntimeError(f"hand-off processes exited with {pn.exitcode}, {po.exitcode}")
             times.append(dt)
         res[mode] = {"seconds": round(statistics.median(times), 4), "tensors": n, "bytes": int(nbytes), "runs": len(times)}
     res["value"] = res["batched-zero-copy"]["seconds"]
     res["speedup_vs_reference_protocol"] = round(res["reference"]["seconds"] / max(res["value"], 1e-9), 1)
     return res
+
+
+if __name__ == "__main__":
+    main()
