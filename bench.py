@@ -148,22 +148,34 @@ def cpu_sample(cfg: ReshardConfig, n_gpus: int):
 
 class OracleSample:
     """A bounded sample of the workload run by the oracle (oracle/restate.py, a restatement of
-    Suika/migration.py:322-556) on host cores; inputs are generated once, outside the timing."""
+    Suika/migration.py:322-556) on host cores; inputs are generated once, outside the timing.
+    N = 1: one layer of cfg2b, both target ranks. N > 1: one target rank's share of two layers
+    (one per target stage, no embeddings): the rank with the most remote ingress, fed by the
+    source ranks it reads from."""
 
     def __init__(self, cfg: ReshardConfig, n_gpus: int, threads: int):
         from oracle import restate as O
         self.O = O
         self.sample = cpu_sample(cfg, n_gpus)
-        self.spl, self.tpl = self.sample.layouts()
-        self.states = S.host_states(self.spl, S.SUBFIELDS, seed=0)
+        self.spl, self.tpl = self.sample.layouts(with_embeddings=(n_gpus == 1))
         self.subs = [(s, k == "meta") for s, k in S.SUBFIELDS]
+        self.threads = threads
         plan = M.Plan(self.spl, self.tpl, minimum_est_peers=1)
+        ops = plan.op_array
         if n_gpus == 1:
             self.units = moved_bytes_views(plan, self.spl, self.tpl)
+            self.ranks = [r for r, m in self.tpl.layout.items() if m]
+            src_ranks = None
+            self.what = self.sample.note
         else:
-            self.units = int(sum(int(o["numel"]) for o in plan.op_array)) * 14
-        self.ranks = [r for r, m in self.tpl.layout.items() if m]
-        self.threads = threads
+            remote = ops["src_rank"] != ops["dst_rank"]
+            ing = {int(r): int(ops["numel"][remote & (ops["dst_rank"] == r)].sum()) for r in np.unique(ops["dst_rank"])}
+            r = max(ing, key=lambda k: (ing[k], -k))
+            self.ranks = [r]
+            src_ranks = sorted(set(int(x) for x in ops["src_rank"][ops["dst_rank"] == r]))
+            self.units = int(ops["numel"][ops["dst_rank"] == r].sum()) * 14
+            self.what = f"target rank {r}'s share of 2 layers (1 per target stage, no embeddings) of {cfg.note}"
+        self.states = S.host_states(self.spl, S.SUBFIELDS, seed=0, ranks=src_ranks, threads=threads)
 
     def step(self) -> float:
         t0 = time.perf_counter()
@@ -174,7 +186,7 @@ class OracleSample:
         return dt
 
     def describe(self, steps: int) -> str:
-        return (f"{self.sample.note}: {self.units / 1e9:.3f} GB of target state per step, {steps} steps, "
+        return (f"{self.what}: {self.units / 1e9:.3f} GB of target state per step, {steps} steps, "
                 f"oracle/restate.py (restatement of Suika/migration.py:322-556) on {self.threads} host threads")
 
 
@@ -535,7 +547,7 @@ def run_reference(args, world):
         "metric": METRIC, "value": round(v, 4), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(t / args.steps * 1e3, 3), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "u8", "data": "synthetic (seeded)", "impl": "reference",
-        "config": {"workload": f"{cfg.name}: {cfg.note} (bounded sample: {smp.sample.note})"},
+        "config": {"workload": f"{cfg.name}: {cfg.note} (bounded sample: {smp.what})"},
         "cpu_baseline": {"value": round(v, 4), "unit": "GB/s", "cores": threads, "kind": "port", "sample": smp.describe(args.steps)},
         "e2e": {"value": round(v, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }

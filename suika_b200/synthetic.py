@@ -91,9 +91,34 @@ def host_shard(full: np.ndarray, tp_meta, rule=None) -> np.ndarray:
 
 
 def host_states(layout, subfields=SUBFIELDS, seed: int = 0, distinct_steps: bool = False,
-                ranks: Optional[Sequence[int]] = None) -> Dict[int, Dict[str, Dict[str, np.ndarray]]]:
-    """rank -> name -> sub-field -> host array for every tensor of a ParamLayout (only `ranks` if given)."""
-    cache: Dict[Tuple[str, str], np.ndarray] = {}
+                ranks: Optional[Sequence[int]] = None, threads: int = 0) -> Dict[int, Dict[str, Dict[str, np.ndarray]]]:
+    """rank -> name -> sub-field -> host array for every tensor of a ParamLayout (only `ranks` if
+    given). Full tensors are drawn on a thread pool (`threads`, default: all cores); `param` is
+    rounded from the `master` draw when both are asked for (the same values host_full gives)."""
+    import os
+    from concurrent.futures import ThreadPoolExecutor
+    wanted: Dict[Tuple[str, str], Tuple[int, ...]] = {}
+    subs = [sub for sub, _ in subfields]
+    for rank, metas in layout.layout.items():
+        if ranks is not None and rank not in ranks:
+            continue
+        for name, m in metas.items():
+            for sub in subs:
+                wanted.setdefault((name, sub), tuple(int(x) for x in m.shape))
+
+    def draw(key):
+        name, sub = key
+        if sub == "param" and (name, "master") in wanted:
+            return None  # rounded from the master draw below
+        return host_full(name, sub, wanted[key], seed, distinct_steps)
+
+    keys = list(wanted)
+    n = threads or (os.cpu_count() or 1)
+    with ThreadPoolExecutor(max_workers=max(1, n)) as ex:
+        cache = dict(zip(keys, ex.map(draw, keys)))
+    for (name, sub), v in list(cache.items()):
+        if v is None:
+            cache[(name, sub)] = bf16_bits(cache[(name, "master")])
     out: Dict[int, Dict[str, Dict[str, np.ndarray]]] = {}
     for rank, metas in layout.layout.items():
         if ranks is not None and rank not in ranks:
@@ -101,11 +126,9 @@ def host_states(layout, subfields=SUBFIELDS, seed: int = 0, distinct_steps: bool
         rs = {}
         for name, m in metas.items():
             ent = {}
-            for sub, _ in subfields:
-                key = (name, sub)
-                if key not in cache:
-                    cache[key] = host_full(name, sub, m.shape, seed, distinct_steps)
-                ent[sub] = cache[key] if sub == "step" else host_shard(cache[key], m.tp_meta, getattr(m, "tp_rule", None))
+            for sub in subs:
+                full = cache[(name, sub)]
+                ent[sub] = full if sub == "step" else host_shard(full, m.tp_meta, getattr(m, "tp_rule", None))
             rs[name] = ent
         out[rank] = rs
     return out
