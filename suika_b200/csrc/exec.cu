@@ -81,6 +81,12 @@ __device__ __forceinline__ uint32_t load_vec(const uint32_t* p) {
 __device__ __forceinline__ uint16_t load_vec(const uint16_t* p) { return __ldg(reinterpret_cast<const unsigned short*>(p)); }
 __device__ __forceinline__ uint8_t load_vec(const uint8_t* p) { return __ldg(reinterpret_cast<const unsigned char*>(p)); }
 
+// Streaming variant: the target is written once (.cs: evict-first store), for copies far larger
+// than L2. (An L2 eviction hint on 16-byte loads does not assemble for sm_100a.)
+__device__ __forceinline__ uint4 load_vec_stream(const uint4* p) { return load_vec(p); }
+__device__ __forceinline__ void store_vec_stream(uint4* p, const uint4& v) {
+  asm volatile("st.global.cs.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w) : "memory");
+}
 __device__ __forceinline__ void store_vec(uint4* p, const uint4& v) {
   asm volatile("st.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w) : "memory");
 }
@@ -90,6 +96,57 @@ __device__ __forceinline__ void store_vec(uint2* p, const uint2& v) {
 __device__ __forceinline__ void store_vec(uint32_t* p, const uint32_t& v) { *p = v; }
 __device__ __forceinline__ void store_vec(uint16_t* p, const uint16_t& v) { *p = v; }
 __device__ __forceinline__ void store_vec(uint8_t* p, const uint8_t& v) { *p = v; }
+
+template <bool STREAM> __device__ __forceinline__ uint4 load16(const uint4* p) { return STREAM ? load_vec_stream(p) : load_vec(p); }
+template <bool STREAM> __device__ __forceinline__ void store16(uint4* p, const uint4& v) {
+  if (STREAM) store_vec_stream(p, v); else store_vec(p, v);
+}
+
+// 16-byte rectangle copy with optional streaming hints (same structure as copy_rect below).
+template <int U, bool STREAM>
+__device__ __forceinline__ void copy_rect16(const char* __restrict__ src, char* __restrict__ dst, uint32_t nr, uint32_t vpr,
+                                            uint64_t sp, uint64_t dp) {
+  const uint32_t total = nr * vpr;
+  const uint32_t stride = blockDim.x;
+  if (nr == 1) {
+    const uint4* s = reinterpret_cast<const uint4*>(src);
+    uint4* d = reinterpret_cast<uint4*>(dst);
+    for (uint32_t base = threadIdx.x; base < total; base += stride * U) {
+      uint4 v[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const uint32_t i = base + u * stride;
+        if (i < total) v[u] = load16<STREAM>(s + i);
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const uint32_t i = base + u * stride;
+        if (i < total) store16<STREAM>(d + i, v[u]);
+      }
+    }
+    return;
+  }
+  const uint32_t sp32 = (uint32_t)sp, dp32 = (uint32_t)dp;
+  for (uint32_t base = threadIdx.x; base < total; base += stride * U) {
+    uint4 v[U];
+    uint32_t doff[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const uint32_t i = base + u * stride;
+      if (i < total) {
+        const uint32_t r = i / vpr;
+        const uint32_t cb = (i - r * vpr) * 16;
+        v[u] = load16<STREAM>(reinterpret_cast<const uint4*>(src + (r * sp32 + cb)));
+        doff[u] = r * dp32 + cb;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const uint32_t i = base + u * stride;
+      if (i < total) store16<STREAM>(reinterpret_cast<uint4*>(dst + doff[u]), v[u]);
+    }
+  }
+}
 
 // Copy an nr x (vpr * VB bytes) rectangle. U loads are issued before their stores. In a
 // multi-row rectangle every in-tile offset fits 32 bits (the host caps rows per tile so that
@@ -219,7 +276,7 @@ struct Schedule {
   }
 };
 
-template <int BLOCK, int U, int MINB>
+template <int BLOCK, int U, int MINB, bool STREAM = false>
 __global__ void __launch_bounds__(BLOCK, MINB) rs_copy_kernel(const DevSeg* __restrict__ segs, int32_t nseg, uint64_t ntiles,
                                                                uint64_t nremote, uint32_t* status) {
   (void)status;  // the vector-copy kernel has no waits that could fail
@@ -229,7 +286,7 @@ __global__ void __launch_bounds__(BLOCK, MINB) rs_copy_kernel(const DevSeg* __re
   while (sch.next(segs, nseg, x)) {
     const uint32_t vpr = (uint32_t)(x.nb >> x.vshift);
     switch (x.vshift) {
-      case 4: copy_rect<16, U>(x.src, x.dst, x.nr, vpr, x.sp, x.dp); break;
+      case 4: copy_rect16<U, STREAM>(x.src, x.dst, x.nr, vpr, x.sp, x.dp); break;
       // Narrow widths only serve entries whose addresses or pitches are not 16-byte aligned
       // (odd shapes); one load in flight per thread keeps their register cost off the main path.
       case 3: copy_rect<8, 1>(x.src, x.dst, x.nr, vpr, x.sp, x.dp); break;
@@ -442,6 +499,7 @@ const Variant kVariants[] = {
     {32, 0, 1, sizeof(TmaA), rs_copy_tma_kernel<8, 16384, 32, 6, 1>},
     {32, 0, 2, sizeof(TmaB), rs_copy_tma_kernel<6, 16384, 32, 4, 2>},
     {32, 0, 1, sizeof(TmaC), rs_copy_tma_kernel<12, 16384, 32, 10, 1>},
+    {256, 8, 2, 0, rs_copy_kernel<256, 8, 2, true>},  // 8: variant 2 with streaming cache hints
 };
 constexpr int kNumVariants = sizeof(kVariants) / sizeof(kVariants[0]);
 

@@ -90,7 +90,7 @@ def test_views_move_only_row_split_pieces():
     assert info.total_bytes == moved + 4 * len([1 for r in (0, 1) for _ in out[r]])  # + one 4-byte step per tensor
 
 
-@pytest.mark.parametrize("variant", ["1", "2", "3", "4", "5", "6", "7"])
+@pytest.mark.parametrize("variant", ["1", "2", "3", "4", "5", "6", "7", "8"])
 @pytest.mark.parametrize("tile", ["256", "4096", "131072"])
 def test_copy_kernel_random_rectangles(tile, variant, monkeypatch):
     """Strided copies with random alignment, pitch and size (every vector width, column-split rows),
