@@ -70,11 +70,25 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gib", type=float, default=2.0)
     ap.add_argument("--variants", default="2,6")
+    ap.add_argument("--one", action="store_true",
+                    help="one pull launch then one push launch on GPU 0 against GPU 1 (for a profiler capture)")
     args = ap.parse_args()
     if torch.cuda.device_count() < 2:
         raise SystemExit("needs two GPUs")
     _enable_peer_access()
     n = int(args.gib * (1 << 30))
+    if args.one:
+        d0, d1 = torch.device("cuda", 0), torch.device("cuda", 1)
+        a0, b0 = torch.ones(n, dtype=torch.uint8, device=d0), torch.empty(n, dtype=torch.uint8, device=d0)
+        a1 = torch.full((n,), 2, dtype=torch.uint8, device=d1)
+        b1 = torch.empty(n, dtype=torch.uint8, device=d1)
+        for name, (s_, d_) in (("pull", (a1, b0)), ("push", (a0, b1))):
+            p = M.PreparedCopies(np.array([_row(s_.data_ptr(), d_.data_ptr(), n, False, 1)], dtype=L.COPY_DESC_DTYPE), d0)
+            p.launch()
+            p.check()
+            assert torch.equal(d_[:1024].cpu(), s_[:1024].cpu())
+            print(f"{name}: {n} bytes copied", flush=True)
+        return
     b = {d: [torch.empty(n, dtype=torch.uint8, device=torch.device("cuda", d)) for _ in range(4)] for d in (0, 1)}
     p = {d: [t.data_ptr() for t in b[d]] for d in (0, 1)}
     for var in args.variants.split(","):
