@@ -14,8 +14,9 @@
  *   - Every function returns an int status: RS_OK (0) or a negative rs_status code.
  *     rs_last_error() returns a message for the last failure on the calling thread.
  *   - No C++ exception crosses this boundary.
- *   - Plans and programs are immutable after build and may be shared between threads;
- *     no global mutable state survives a call except the per-thread error message.
+ *   - Plans and programs are immutable after build and may be shared between threads. The only
+ *     state kept across calls is the per-thread error message and, for
+ *     rs_copy_launch_noalloc, its built-in device table and the per-device address of it.
  *   - Pointers named *_dev are device addresses; everything else is host memory.
  */
 #ifndef SUIKA_RESHARD_H

@@ -463,35 +463,48 @@ def _check_source(t: torch.Tensor, name: str, sub: str, device: torch.device, dt
 
 
 class _MetaStage:
-    """Singleton sub-fields: values gathered on the host, uploaded once, and written into their
-    own target tensors by 4-byte entries of the same copy table."""
+    """Singleton sub-fields (e.g. Adam's step), written into their own target tensors by entries
+    of the same copy table: values already on the target device are copied device to device;
+    host values are gathered, uploaded once, and copied from the staging buffer."""
 
     def __init__(self, device: torch.device):
         self.device = device
         self.values: List[bytes] = []
         self.targets: List[torch.Tensor] = []
+        self.direct: List[Tuple[int, torch.Tensor, int]] = []  # (source address, target, bytes)
+        self._keep: List[torch.Tensor] = []
 
     def add(self, value: torch.Tensor, out: torch.Tensor) -> None:
         v = value.detach().reshape(-1)
         if v.numel() != 1 or v.element_size() != out.element_size():
             raise AssertionError(f"singleton sub-field of {v.numel()} x {v.dtype} cannot fill {out.dtype}")
+        if v.device == out.device:
+            v = v.contiguous()
+            self._keep.append(v)
+            self.direct.append((v.data_ptr(), out, v.element_size()))
+            return
         self.values.append(v.cpu().view(torch.uint8).numpy().tobytes())
         self.targets.append(out)
 
-    def descs(self) -> Tuple[np.ndarray, Optional[torch.Tensor]]:
+    def descs(self) -> Tuple[np.ndarray, Optional[List[torch.Tensor]]]:
+        """The copy entries and the buffers they read, which must outlive the launches."""
+        d = np.zeros(len(self.targets) + len(self.direct), dtype=L.COPY_DESC_DTYPE)
+        for i, (src, t, n) in enumerate(self.direct):
+            d[i] = (src, t.data_ptr(), 1, n, n, n, 0)
         if not self.targets:
-            return np.zeros(0, dtype=L.COPY_DESC_DTYPE), None
+            return d, (list(self._keep) if self._keep else None)
         sizes = [len(v) for v in self.values]
         offs = np.cumsum([0] + [(s + 15) // 16 * 16 for s in sizes])
         host = np.zeros(int(offs[-1]), dtype=np.uint8)
         for o, v in zip(offs, self.values):
             host[o:o + len(v)] = np.frombuffer(v, dtype=np.uint8)
         stage = torch.from_numpy(host).to(self.device)
-        d = np.zeros(len(self.targets), dtype=L.COPY_DESC_DTYPE)
         base = stage.data_ptr()
+        k = len(self.direct)
         for i, (o, s, t) in enumerate(zip(offs, sizes, self.targets)):
-            d[i] = (base + int(o), t.data_ptr(), 1, s, s, s, 0)
-        return d, stage
+            d[k + i] = (base + int(o), t.data_ptr(), 1, s, s, s, 0)
+        self._keep.append(stage)
+        return d, list(self._keep)
 
 
 def _meta_target(value: torch.Tensor, first_is_self: bool, field_type, device: torch.device) -> torch.Tensor:
@@ -577,7 +590,8 @@ def reshard_local(source_param_layout, target_param_layout, source_state_dicts: 
     prepared = PreparedCopies(table, device, stream) if len(table) else None
     info = prepared.launch(stream) if prepared is not None else L.RsLaunchInfo()
     if stage is not None and stream is not None:
-        stage.record_stream(stream)
+        for t in stage:
+            t.record_stream(stream)
     if return_info:
         return out, info, prepared
     return out

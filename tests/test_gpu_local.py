@@ -16,9 +16,10 @@ pytestmark = pytest.mark.gpu
 DEV = torch.device("cuda", 0)
 
 
-def to_device(states):
+def to_device(states, step_on_device: bool = False):
     kinds = dict(SUBS)
-    return {r: {n: {s: S.to_torch(a, kinds[s], DEV if kinds[s] != "meta" else None) for s, a in ent.items()}
+    return {r: {n: {s: S.to_torch(a, kinds[s], DEV if (kinds[s] != "meta" or step_on_device) else None)
+                    for s, a in ent.items()}
                 for n, ent in st.items()} for r, st in states.items()}
 
 
@@ -29,14 +30,17 @@ def host(t: torch.Tensor) -> np.ndarray:
     return t.numpy()
 
 
-@pytest.mark.parametrize("case", sorted(CASES))
-def test_reshard_local_matches_reference_digests(case):
+@pytest.mark.parametrize("case,step_on_device",
+                         [(c, False) for c in sorted(CASES)] + [("cfg3_mini", True), ("odd_mini", True)])
+def test_reshard_local_matches_reference_digests(case, step_on_device):
+    """step_on_device: Adam's step lives in HBM (fused/capturable optimisers); it is then copied
+    device to device by the same launch instead of being staged from the host."""
     g = load_golden(case)
     cfg = CASES[case]["config"]
     spl, tpl = cfg.layouts()
     states = golden_states(cfg, seed=g["seed"])
     plan = M.Plan(spl, tpl, minimum_est_peers=g["minimum_est_peers"])
-    out = M.reshard_local(spl, tpl, to_device(states), S.expected_sub_fields(), DEV, plan=plan)
+    out = M.reshard_local(spl, tpl, to_device(states, step_on_device), S.expected_sub_fields(), DEV, plan=plan)
     torch.cuda.synchronize()
     for rank_s, want in g["ranks"].items():
         got = out[int(rank_s)]
