@@ -323,6 +323,67 @@ int rs_peer_export(const void* ptr_dev, rs_peer_handle* out, uint64_t* offset);
 int rs_peer_open(const rs_peer_handle* handle, void** base_dev);
 int rs_peer_close(void* base_dev);
 
+/* ---- activation exchange between pipeline stages ----------------------------------------
+ * Replaces the cross-stage send/recv of PipelineExecModule (Suika/pipeline_parallel.py:665-836):
+ * per rank, a list of P2P ops built by _get_recv_or_send_P2P_ops (:665-776), each staging a
+ * .contiguous() copy of a (batch range x slice chunk) block (:748-756) and copying it back after
+ * the transfer, followed on the receive side by a TP all-gather and a cat (:817-832). Here every
+ * receiver's complete tensor is planned as pieces that one copy launch (rs_copy_launch) writes
+ * straight into place: no staging copies, no all-gather, no cat. Bytes written are the ones the
+ * reference delivers, from the same sender. */
+
+/* One stage's DeviceMesh2D (Suika/device_mesh.py:150-240) with its local batch sizes
+ * (lbsz_mesh[stage], pipeline_parallel.py:175): DP group g is the TP group
+ * ranks[group_start[g] .. group_start[g + 1]); groups hold batch rows in group order. */
+typedef struct rs_stage_mesh {
+  int32_t n_groups;
+  int32_t reserved;
+  const int32_t* group_start; /* n_groups + 1 offsets into ranks   */
+  const int32_t* ranks;
+  const int64_t* local_bsz;   /* local batch size of each DP group */
+} rs_stage_mesh;
+
+/* One block a receiver gets: batch rows [dst_batch, dst_batch + n_batch) of its local tensor
+ * (rows [src_batch, ...) of the sender's) by slice-dim range [slice_start, slice_start + slice_len). */
+typedef struct rs_act_piece {
+  int32_t src_rank;
+  int32_t dst_rank;
+  int64_t src_batch;
+  int64_t dst_batch;
+  int64_t n_batch;
+  int64_t slice_start;
+  int64_t slice_len;
+} rs_act_piece;
+
+/* Layout of every rank's activation tensor (contiguous, row-major). shape[batch_dim] is ignored:
+ * each rank's own local batch size applies. batch_dim and slice_dim are non-negative and differ. */
+typedef struct rs_act_geometry {
+  int32_t ndim;
+  int32_t batch_dim;
+  int32_t slice_dim;
+  int32_t elem_bytes;
+  int64_t shape[RS_MAX_DIMS];
+} rs_act_geometry;
+
+/* Every piece from stage src to stage dst, receiver by receiver (DP group, then TP index), then
+ * sending DP group, then slice position. Sends only where the batch ranges overlap
+ * (pipeline_parallel.py:711-721). Along the slice dim an overlap is cut into k = max(s, d)
+ * chunks, s and d the two groups' TP degrees (powers of two, else RS_ERR_SHAPE); chunk c comes
+ * from TP rank c * s / k of the sending group. slice_size % k != 0 is RS_ERR_SHAPE. out == NULL
+ * only counts: *n_out = number of pieces. */
+int rs_act_plan(const rs_stage_mesh* src, const rs_stage_mesh* dst, int64_t slice_size,
+                rs_act_piece* out, int64_t capacity, int64_t* n_out);
+
+/* Copy descriptors of pieces. src_dev[r] / dst_dev[r]: base address of rank r's sending /
+ * receiving tensor in this process (r < n_ranks; a piece whose address is 0 is RS_ERR_ARG).
+ * A piece becomes prod(shape[:min(batch_dim, slice_dim)]) descriptors; pieces that leave a
+ * rank's tensor are RS_ERR_BOUNDS. RS_COPY_REMOTE is set when the two ranks differ. out == NULL
+ * only counts. */
+int rs_act_resolve(const rs_stage_mesh* src, const rs_stage_mesh* dst, const rs_act_geometry* geometry,
+                   const rs_act_piece* pieces, int64_t n_pieces,
+                   const uint64_t* src_dev, const uint64_t* dst_dev, int32_t n_ranks,
+                   rs_copy_desc* out, int64_t capacity, int64_t* n_out);
+
 #ifdef __cplusplus
 }
 #endif

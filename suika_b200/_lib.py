@@ -112,6 +112,21 @@ class RsPeerHandle(C.Structure):
                 ("device", C.c_int32), ("pid", C.c_int32)]
 
 
+class RsStageMesh(C.Structure):
+    _fields_ = [("n_groups", C.c_int32), ("reserved", C.c_int32), ("group_start", C.POINTER(C.c_int32)),
+                ("ranks", C.POINTER(C.c_int32)), ("local_bsz", C.POINTER(C.c_int64))]
+
+
+class RsActPiece(C.Structure):
+    _fields_ = [("src_rank", C.c_int32), ("dst_rank", C.c_int32), ("src_batch", C.c_int64), ("dst_batch", C.c_int64),
+                ("n_batch", C.c_int64), ("slice_start", C.c_int64), ("slice_len", C.c_int64)]
+
+
+class RsActGeometry(C.Structure):
+    _fields_ = [("ndim", C.c_int32), ("batch_dim", C.c_int32), ("slice_dim", C.c_int32), ("elem_bytes", C.c_int32),
+                ("shape", C.c_int64 * RS_MAX_DIMS)]
+
+
 # numpy mirrors used to fill large descriptor arrays without a Python loop per field.
 TENSOR_META_DTYPE = np.dtype([("name_id", "<i4"), ("ndim", "<i4"), ("shape", "<i8", (RS_MAX_DIMS,)),
                               ("itemsize", "<i4"), ("slice_dim", "<i4"), ("tp_index", "<i4"), ("tp_deg", "<i4")])
@@ -119,7 +134,10 @@ COPY_DESC_DTYPE = np.dtype([("src_dev", "<u8"), ("dst_dev", "<u8"), ("rows", "<u
                             ("src_pitch", "<u8"), ("dst_pitch", "<u8"), ("flags", "<u8")])
 SEGMENT_DTYPE = np.dtype([("src_slot", "<i4"), ("dst_slot", "<i4"), ("src_offset", "<u8"), ("dst_offset", "<u8"),
                           ("rows", "<u8"), ("row_bytes", "<u8"), ("src_pitch", "<u8"), ("dst_pitch", "<u8")])
+ACT_PIECE_DTYPE = np.dtype([("src_rank", "<i4"), ("dst_rank", "<i4"), ("src_batch", "<i8"), ("dst_batch", "<i8"),
+                            ("n_batch", "<i8"), ("slice_start", "<i8"), ("slice_len", "<i8")])
 assert TENSOR_META_DTYPE.itemsize == C.sizeof(RsTensorMeta)
+assert ACT_PIECE_DTYPE.itemsize == C.sizeof(RsActPiece)
 assert COPY_DESC_DTYPE.itemsize == C.sizeof(RsCopyDesc)
 assert SEGMENT_DTYPE.itemsize == C.sizeof(RsSegment)
 
@@ -154,6 +172,10 @@ SIGNATURES = {
     "rs_peer_export": (C.c_int, [_P, C.POINTER(RsPeerHandle), C.POINTER(C.c_uint64)]),
     "rs_peer_open": (C.c_int, [C.POINTER(RsPeerHandle), C.POINTER(_P)]),
     "rs_peer_close": (C.c_int, [_P]),
+    "rs_act_plan": (C.c_int, [C.POINTER(RsStageMesh), C.POINTER(RsStageMesh), C.c_int64, _P, C.c_int64,
+                              C.POINTER(C.c_int64)]),
+    "rs_act_resolve": (C.c_int, [C.POINTER(RsStageMesh), C.POINTER(RsStageMesh), C.POINTER(RsActGeometry), _P, C.c_int64,
+                                 _P, _P, C.c_int32, _P, C.c_int64, C.POINTER(C.c_int64)]),
 }
 
 _lock = threading.Lock()

@@ -15,7 +15,7 @@ REPO_DIR = os.path.dirname(PKG_DIR)
 CSRC = os.path.join(PKG_DIR, "csrc")
 LIB_NAME = "libsuika_reshard.so"
 LIB_PATH = os.path.join(PKG_DIR, LIB_NAME)
-SOURCES = [os.path.join(CSRC, "plan.cpp"), os.path.join(CSRC, "exec.cu")]
+SOURCES = [os.path.join(CSRC, "plan.cpp"), os.path.join(CSRC, "act.cpp"), os.path.join(CSRC, "exec.cu")]
 DEPS = SOURCES + [os.path.join(CSRC, "internal.h"), os.path.join(REPO_DIR, "include", "suika_reshard.h")]
 
 NVCC_FLAGS = [

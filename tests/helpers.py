@@ -73,3 +73,23 @@ def emulate_program(prog, names, states, rank) -> Dict[str, Dict[str, np.ndarray
         out.setdefault(name, {})[sub] = v if ms["first_is_self"] else v.reshape(1)
     # sub-fields in expected order
     return {n: {s: ent[s] for s, _ in SUBS if s in ent} for n, ent in out.items()}
+
+
+class Memory:
+    """Flat emulated address space: named buffers at fixed, non-overlapping base addresses."""
+
+    def __init__(self):
+        self.bufs = []  # (base, bytearray-like numpy uint8)
+        self.next = 1 << 20
+
+    def add(self, arr: np.ndarray) -> int:
+        base = self.next
+        self.bufs.append((base, arr))
+        self.next += (arr.nbytes + (1 << 12)) // 256 * 256 + 256
+        return base
+
+    def view(self, addr, n):
+        for base, a in self.bufs:
+            if base <= addr and addr + n <= base + a.nbytes:
+                return a[addr - base: addr - base + n]
+        raise AssertionError(f"address {addr:#x}+{n} outside every buffer")

@@ -7,30 +7,10 @@ import pytest
 
 from suika_b200 import migration as M
 from tests.golden.cases import CASES
-from tests.helpers import SUB_ITEMSIZE, SUBS, digest, golden_states, load_golden
+from tests.helpers import SUB_ITEMSIZE, SUBS, Memory, digest, golden_states, load_golden
 
 SPEC = [(SUB_ITEMSIZE[s], kind == "meta") for s, kind in SUBS]
 SUBNAMES = [s for s, _ in SUBS]
-
-
-class Memory:
-    """Flat emulated address space: named buffers at fixed, non-overlapping base addresses."""
-
-    def __init__(self):
-        self.bufs = []  # (base, bytearray-like numpy uint8)
-        self.next = 1 << 20
-
-    def add(self, arr: np.ndarray) -> int:
-        base = self.next
-        self.bufs.append((base, arr))
-        self.next += (arr.nbytes + (1 << 12)) // 256 * 256 + 256
-        return base
-
-    def view(self, addr, n):
-        for base, a in self.bufs:
-            if base <= addr and addr + n <= base + a.nbytes:
-                return a[addr - base: addr - base + n]
-        raise AssertionError(f"address {addr:#x}+{n} outside every buffer")
 
 
 def run_push(case):
