@@ -568,6 +568,8 @@ def main():
     ap.add_argument("--no-check", action="store_true")
     ap.add_argument("--no-phases", action="store_true", help="N > 1: run all transfers at once instead of in matching phases")
     ap.add_argument("--handoff", action="store_true", help="time the old -> new process hand-off instead (1 GPU)")
+    ap.add_argument("--activation", action="store_true",
+                    help="time the pipeline activation hand-over between two stages instead (N >= 2 under torchrun)")
     ap.add_argument("--direction", choices=["pull", "push"], default="push",
                     help="N > 1: target ranks read their pieces (pull) or source ranks write them (push)")
     args = ap.parse_args()
@@ -577,6 +579,19 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     if args.handoff:
         print(json.dumps(run_handoff(args)), flush=True)
+        return
+    if args.activation:
+        import datetime
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", rank)))
+        os.environ.setdefault("NCCL_DEBUG", "WARN")
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+        try:
+            res = run_activation(args)
+        finally:
+            dist.barrier()
+            dist.destroy_process_group()
+        if res is not None:
+            print(json.dumps(res), flush=True)
         return
     if args.impl == "reference":
         if rank == 0:
@@ -701,6 +716,155 @@ def run_handoff(args):
         res[mode] = {"seconds": round(statistics.median(times), 4), "tensors": n, "bytes": int(nbytes), "runs": len(times)}
     res["value"] = res["batched-zero-copy"]["seconds"]
     res["speedup_vs_reference_protocol"] = round(res["reference"]["seconds"] / max(res["value"], 1e-9), 1)
+    return res
+
+
+# ---------------------------------------------------------------------------------------------
+# --activation: pipeline activation hand-over between two stages (N GPUs under torchrun)
+# ---------------------------------------------------------------------------------------------
+ACT_BATCH, ACT_SEQ, ACT_HIDDEN = 8, 2048, 5120
+
+
+def activation_stages(world: int):
+    """Stage A: the first N/2 ranks as one TP group; stage B: the other N/2 as DP N/2 x TP1 (the
+    boundary a TP -> DP re-plan makes). Global micro-batch 8 x 2048 tokens, hidden 5120 (13B), bf16."""
+    half = world // 2
+    return [list(range(half))], [ACT_BATCH], [[half + i] for i in range(half)], [ACT_BATCH // half] * half
+
+
+def _ref_port_exchange(rank, mesh_s, mesh_d, bsz_s, bsz_d, act, target, tp_groups):
+    """The reference's sequence for one direction (Suika/pipeline_parallel.py:687-836, with
+    Suika/utils.py:212-234): per block a .contiguous() staging copy, non-batched isend/irecv
+    (sends first), copy back into place, then the receiving TP group's all-gather + cat + copy."""
+    from oracle import activation as OA
+    sends, recvs, restore = [], [], []
+    if act is not None:
+        for peer, b0, nb, deg, tr in OA.p2p_ops(rank, mesh_s, mesh_d, bsz_s, bsz_d, "send"):
+            c = act.shape[-1] // deg
+            sends.append((act.narrow(0, b0, nb).narrow(-1, tr * c, c).contiguous(), peer))
+    if target is not None:
+        for peer, b0, nb, deg, tr in OA.p2p_ops(rank, mesh_s, mesh_d, bsz_s, bsz_d, "recv"):
+            c = target.shape[-1] // deg
+            view = target.narrow(0, b0, nb).narrow(-1, tr * c, c)
+            buf = view.contiguous()
+            recvs.append((buf, peer))
+            restore.append((view, buf))
+    reqs = [dist.isend(t, dst=p) for t, p in sends] + [dist.irecv(t, src=p) for t, p in recvs]
+    for q in reqs:
+        q.wait()
+    for view, buf in restore:
+        view.copy_(buf)
+    if target is not None:
+        for group, pg in tp_groups:
+            if rank in group and len(group) > 1:
+                j = group.index(rank)
+                part = target.chunk(len(group), dim=-1)[j]
+                parts = [torch.empty_like(part) for _ in group]
+                dist.all_gather(parts, part.contiguous(), group=pg)
+                target.copy_(torch.cat(parts, dim=-1))
+
+
+def run_activation(args):
+    from suika_b200 import activation as A
+    rank, world = dist.get_rank(), dist.get_world_size()
+    if world < 2 or world % 2 or ACT_BATCH % (world // 2):
+        raise SystemExit("--activation needs an even number of ranks (2, 4 or 8)")
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", rank)))
+    ma, ba, mb, bb = activation_stages(world)
+    shape, dtype = [-1, ACT_SEQ, ACT_HIDDEN], torch.bfloat16
+    in_a = rank in ma[0]
+    in_b = not in_a
+
+    def mine(rows: int) -> torch.Tensor:
+        g = torch.Generator(dev).manual_seed(rank)
+        return torch.randn(rows, ACT_SEQ, ACT_HIDDEN, device=dev, generator=g).to(dtype)
+    b_rows = bb[0]
+    act_f = mine(ACT_BATCH) if in_a else None           # forward: A sends, B receives
+    act_b = mine(b_rows) if in_b else None              # backward: B sends, A receives
+    tgt_f = torch.zeros(b_rows, ACT_SEQ, ACT_HIDDEN, dtype=dtype, device=dev) if in_b else None
+    tgt_b = torch.zeros(ACT_BATCH, ACT_SEQ, ACT_HIDDEN, dtype=dtype, device=dev) if in_a else None
+    tp_groups = [(g, dist.new_group(g)) for g in ma + mb]  # every rank creates every group
+    if args.impl == "reference":
+        def step():
+            _ref_port_exchange(rank, ma, mb, ba, bb, act_f, tgt_f, tp_groups)
+            _ref_port_exchange(rank, mb, ma, bb, ba, act_b, tgt_b, tp_groups)
+        launches = None
+    else:
+        fwd = A.ActivationExchange(rank, ma, mb, ba, bb, shape, dtype, device=dev)
+        bwd = A.ActivationExchange(rank, mb, ma, bb, ba, shape, dtype, device=dev)
+
+        def step():
+            fwd.exchange(act_f, tgt_f)
+            bwd.exchange(act_b, tgt_b)
+        launches = 2  # per rank and step: one send launch in one direction, one receive copy in the other
+    with Clocks(dev.index) as ck:
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize()
+        dist.barrier()
+        times = []
+        for _ in range(args.steps):
+            dist.barrier()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            step()
+            b.record()
+            torch.cuda.synchronize()
+            times.append(a.elapsed_time(b))
+        dist.barrier()
+    check = {"status": "skipped"}
+    if args.impl != "reference":
+        # the same inputs through the reference's sequence must give the same bytes
+        ref_f = torch.zeros_like(tgt_f) if tgt_f is not None else None
+        ref_b = torch.zeros_like(tgt_b) if tgt_b is not None else None
+        _ref_port_exchange(rank, ma, mb, ba, bb, act_f, ref_f, tp_groups)
+        _ref_port_exchange(rank, mb, ma, bb, ba, act_b, ref_b, tp_groups)
+        torch.cuda.synchronize()
+        ok = all(torch.equal(x, y) for x, y in ((tgt_f, ref_f), (tgt_b, ref_b)) if x is not None)
+        flags = [None] * world
+        dist.all_gather_object(flags, ok)
+        check = {"status": "pass" if all(flags) else "FAIL", "what": "every received tensor equals the reference sequence's"}
+        fwd.check()
+        bwd.check()
+        fwd.close()
+        bwd.close()
+    per_rank = [None] * world
+    dist.all_gather_object(per_rank, round(statistics.mean(times), 4))
+    t = max(per_rank) / 1e3
+    elem = 2
+    fwd_bytes = ACT_BATCH * ACT_SEQ * ACT_HIDDEN * elem            # every B rank gets its rows once
+    bwd_bytes = len(ma[0]) * ACT_BATCH * ACT_SEQ * ACT_HIDDEN * elem  # every A rank gets the whole batch
+    pf = A.plan_activation_exchange(ma, mb, ba, bb, ACT_HIDDEN)
+    pb = A.plan_activation_exchange(mb, ma, bb, ba, ACT_HIDDEN)
+    io = {}
+    for pcs in (pf, pb):
+        for p in pcs:
+            nb = int(p["n_batch"]) * ACT_SEQ * int(p["slice_len"]) * elem
+            if p["src_rank"] != p["dst_rank"]:
+                io.setdefault(int(p["src_rank"]), [0, 0])[1] += nb
+                io.setdefault(int(p["dst_rank"]), [0, 0])[0] += nb
+    max_dir = max(max(v) for v in io.values())
+    if rank != 0:
+        return None
+    res = {
+        "metric": "pipeline activation hand-over between stages (forward + backward per micro-batch)",
+        "value": round((fwd_bytes + bwd_bytes) / t / 1e9, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(t * 1e3, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded normal activations)",
+        "config": {"workload": f"stage A TP{len(ma[0])} -> stage B DP{len(mb)} x TP1 and back; micro-batch "
+                               f"{ACT_BATCH} x {ACT_SEQ} tokens, hidden {ACT_HIDDEN}, bf16",
+                   "received_mb_per_step": round((fwd_bytes + bwd_bytes) / 1e6, 1),
+                   "l2": "buffers reused each step; per-step bytes above L2 only at N >= 4"},
+        "roofline": {"bound": "nvlink", "achieved": round(max_dir / t / 1e9, 1), "peak": NVLINK_PEER_GBS, "unit": "GB/s",
+                     "frac": round(max_dir / t / 1e9 / NVLINK_PEER_GBS, 4), "algorithmic_bytes_per_step": int(max_dir),
+                     "peak_source": "measured peer copy per direction per GPU on this pool (900 GB/s nominal)", "traffic": None},
+        "per_rank_ms": per_rank, "clocks": ck.summary(), "check": check,
+    }
+    if launches is not None:
+        res["gpu_launches"] = launches * args.steps
+    if args.impl == "reference":
+        res["impl"] = "reference"
+        res["reference_kind"] = "port of the reference's NCCL sequence (torch.distributed isend/irecv + all_gather)"
     return res
 
 
