@@ -216,17 +216,17 @@ class ActivationExchange:
         if self.is_receiver:
             self._window = torch.zeros([slots, *self.my_dst_shape], dtype=dtype, device=self.device)
             handles, where = _export([self._window])
-            mine = {"handle": handles[0], "offset": where[0][1]}
+            mine = {"handle": handles[0], "offset": where[0][1], "slot_bytes": self._slot_bytes}
         everyone: List[Dict[str, object]] = [None] * dist.get_world_size(group)  # type: ignore[list-item]
         dist.all_gather_object(everyone, (self.rank, mine), group=group)
-        self._remote_window: Dict[int, int] = {}
+        self._remote_window: Dict[int, Tuple[int, int]] = {}  # receiver -> (window address here, slot bytes)
         if self.is_sender:
             wanted = set(int(r) for r in self.pieces["dst_rank"][self.pieces["src_rank"] == self.rank])
             with torch.cuda.device(self.device):
                 for r, info in everyone:
                     if r in wanted:
                         base = self._peers.base(r, 0, info["handle"])
-                        self._remote_window[r] = base + int(info["offset"])
+                        self._remote_window[r] = (base + int(info["offset"]), int(info["slot_bytes"]))
             missing = wanted - set(self._remote_window)
             if missing:
                 raise AssertionError(f"receivers {sorted(missing)} did not publish a window")
@@ -262,7 +262,8 @@ class ActivationExchange:
         key = (activation.data_ptr(), slot)
         table = self._tables.get(key, False)
         if table is False:
-            windows = {r: base + slot * self._slot_bytes for r, base in self._remote_window.items()}
+            # each receiver's slot stride is its own tensor's size (published with its window)
+            windows = {r: base + slot * stride for r, (base, stride) in self._remote_window.items()}
             descs = send_table(self.src, self.dst, self.geo, self.pieces, self.rank, activation.data_ptr(), windows)
             table = self._remember(key, descs)
         if table is not None:

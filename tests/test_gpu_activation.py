@@ -82,7 +82,7 @@ def _worker(rank, world, name, port, outdir):
         from suika_b200 import activation as A
         torch.cuda.set_device(rank)
         dev = torch.device("cuda", rank)
-        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120))
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=45))
         case = DIST_CASES[name]
         back = dict(case, mesh_src=case["mesh_dst"], bszs_src=case["bszs_dst"], mesh_dst=case["mesh_src"], bszs_dst=case["bszs_src"])
         tdtype = torch.bfloat16 if case["dtype"] == "bfloat16" else torch.float32
