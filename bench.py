@@ -836,14 +836,17 @@ def run_activation(args):
     bwd_bytes = len(ma[0]) * ACT_BATCH * ACT_SEQ * ACT_HIDDEN * elem  # every A rank gets the whole batch
     pf = A.plan_activation_exchange(ma, mb, ba, bb, ACT_HIDDEN)
     pb = A.plan_activation_exchange(mb, ma, bb, ba, ACT_HIDDEN)
-    io = {}
+    # the two directions run one after the other: the step's NVLink bound is the sum over them of
+    # the busiest GPU direction (ingress or egress) of each
+    max_dir = 0
     for pcs in (pf, pb):
+        io = {}
         for p in pcs:
             nb = int(p["n_batch"]) * ACT_SEQ * int(p["slice_len"]) * elem
             if p["src_rank"] != p["dst_rank"]:
                 io.setdefault(int(p["src_rank"]), [0, 0])[1] += nb
                 io.setdefault(int(p["dst_rank"]), [0, 0])[0] += nb
-    max_dir = max(max(v) for v in io.values())
+        max_dir += max(max(v) for v in io.values())
     if rank != 0:
         return None
     res = {
