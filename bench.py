@@ -568,6 +568,8 @@ def main():
     ap.add_argument("--no-check", action="store_true")
     ap.add_argument("--no-phases", action="store_true", help="N > 1: run all transfers at once instead of in matching phases")
     ap.add_argument("--handoff", action="store_true", help="time the old -> new process hand-off instead (1 GPU)")
+    ap.add_argument("--metadata", action="store_true",
+                    help="time the layout exchange before a reshard instead (N ranks under torchrun; gloo without GPUs)")
     ap.add_argument("--activation", action="store_true",
                     help="time the pipeline activation hand-over between two stages instead (N >= 2 under torchrun)")
     ap.add_argument("--direction", choices=["pull", "push"], default="push",
@@ -579,6 +581,19 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     if args.handoff:
         print(json.dumps(run_handoff(args)), flush=True)
+        return
+    if args.metadata:
+        backend = "nccl" if torch.cuda.is_available() else "gloo"
+        if backend == "nccl":
+            torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", rank)))
+        dist.init_process_group(backend)
+        try:
+            res = run_metadata(args)
+        finally:
+            dist.barrier()
+            dist.destroy_process_group()
+        if res is not None:
+            print(json.dumps(res), flush=True)
         return
     if args.activation:
         import datetime
@@ -869,6 +884,55 @@ def run_activation(args):
         res["impl"] = "reference"
         res["reference_kind"] = "port of the reference's NCCL sequence (torch.distributed isend/irecv + all_gather)"
     return res
+
+
+# ---------------------------------------------------------------------------------------------
+# --metadata: the layout exchange before a reshard (N ranks under torchrun; gloo without GPUs)
+# ---------------------------------------------------------------------------------------------
+def run_metadata(args):
+    """What precedes the copies of a reshard: both layouts gathered from every rank, then the plan.
+    The reference gathers {name: TensorMeta} objects with all_gather_object (ParamLayout.gather,
+    Suika/migration.py:172-192) and plans from them; suika_b200.metadata gathers records
+    (gather_param_layout) and plans from the records. cfg3's layouts when the world has 8 ranks,
+    otherwise the Llama2-13B TP N -> TP N/2 x PP2 layouts."""
+    from suika_b200 import metadata as MD
+    rank, world = dist.get_rank(), dist.get_world_size()
+    cfg = CONFIGS["cfg3"] if world == 8 else workload(world)
+    spl, tpl = cfg.layouts()
+    src_mine, dst_mine = spl.layout.get(rank, {}), tpl.layout.get(rank, {})
+    ref_t, ours_t = [], []
+    for i in range(args.warmup + args.steps):
+        dist.barrier()
+        t0 = time.perf_counter()
+        layouts = []
+        for mine in (src_mine, dst_mine):
+            objs = [None] * world
+            dist.all_gather_object(objs, mine)
+            pl = M.ParamLayout()
+            pl.layout = dict(enumerate(objs))
+            layouts.append(pl)
+        ref_plan = M.Plan(*layouts, minimum_est_peers=1)
+        t1 = time.perf_counter()
+        dist.barrier()
+        t2 = time.perf_counter()
+        ours_plan = M.Plan(MD.gather_param_layout(src_mine), MD.gather_param_layout(dst_mine), minimum_est_peers=1)
+        t3 = time.perf_counter()
+        if i >= args.warmup:
+            ref_t.append(t1 - t0)
+            ours_t.append(t3 - t2)
+        if i == 0 and not np.array_equal(ref_plan.op_array, ours_plan.op_array):
+            raise RuntimeError("plans from records and from objects differ")
+    stats = [None] * world
+    dist.all_gather_object(stats, [statistics.median(ref_t), statistics.median(ours_t)])
+    if rank != 0:
+        return None
+    ref_s, ours_s = max(s[0] for s in stats), max(s[1] for s in stats)
+    return {"metric": "layout exchange and planning before a reshard (s, max over ranks, median of steps)", "unit": "s",
+            "higher_is_better": False, "backend": dist.get_backend(), "world": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "config": {"workload": f"{cfg.name} source and target layouts, {len(src_mine)} tensors on rank 0 before"},
+            "value": round(ours_s, 6), "reference_objects_s": round(ref_s, 6), "records_s": round(ours_s, 6),
+            "speedup": round(ref_s / ours_s, 2), "check": "plans equal"}
 
 
 if __name__ == "__main__":

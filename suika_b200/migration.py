@@ -209,6 +209,14 @@ def _flatten_layout(layout: Dict[int, Dict[str, Any]], name_ids: Dict[str, int],
     return ranks, arrays
 
 
+def _flatten_any(param_layout, name_ids: Dict[str, int], names: List[str], rules: Optional[Dict[str, Any]] = None):
+    """A layout's records for the planner: a CompactLayout (suika_b200.metadata) hands over its
+    records as they are; a ParamLayout's objects are read one by one."""
+    if hasattr(param_layout, "flatten"):
+        return param_layout.flatten(name_ids, names, rules)
+    return _flatten_layout(param_layout.layout, name_ids, names, rules)
+
+
 def _rank_layouts(ranks, arrays):
     out = (L.RsRankLayout * max(1, len(ranks)))()
     for i, (r, a) in enumerate(zip(ranks, arrays)):
@@ -234,8 +242,8 @@ class Plan:
         self.names: List[str] = []
         self.name_ids: Dict[str, int] = {}
         rules: Dict[str, Any] = {}
-        s_ranks, s_arr = _flatten_layout(source_param_layout.layout, self.name_ids, self.names, rules)
-        d_ranks, d_arr = _flatten_layout(target_param_layout.layout, self.name_ids, self.names, rules)
+        s_ranks, s_arr = _flatten_any(source_param_layout, self.name_ids, self.names, rules)
+        d_ranks, d_arr = _flatten_any(target_param_layout, self.name_ids, self.names, rules)
         self.src_ranks, self.dst_ranks = s_ranks, d_ranks
         # "reference": the reference's schedule and cat order (chunk layouts only). "interval": slice
         # intersection, slice order, balanced replicas (any slice rules). "auto": interval iff rules.
