@@ -368,7 +368,12 @@ def run_dist(args):
     exp = S.expected_sub_fields()
     plan = M.Plan(spl, tpl, minimum_est_peers=1)
     src = {n: dict(e) for n, e in state.state.items()}
-    rt = (M.RankTransfer if args.direction == "pull" else M.RankTransferPush)(plan, src, exp, dev, phased=not args.no_phases)
+    if args.direction == "pull":
+        rt = M.RankTransfer(plan, src, exp, dev, phased=not args.no_phases)
+    else:
+        from suika_b200.fanout import plan_fanout
+        fo = plan_fanout(plan, sum([2, 4, 4, 4]), mode={"off": False, "auto": "auto", "on": True}[args.fanout])
+        rt = M.RankTransferPush(plan, src, exp, dev, phased=not args.no_phases, fanout=fo if fo.active else None)
     its = [2, 4, 4, 4]
     rb = plan.rank_bytes(its)
     moved_all = int(plan.op_array["numel"].sum()) * sum(its)
@@ -572,6 +577,8 @@ def main():
                     help="time the layout exchange before a reshard instead (N ranks under torchrun; gloo without GPUs)")
     ap.add_argument("--activation", action="store_true",
                     help="time the pipeline activation hand-over between two stages instead (N >= 2 under torchrun)")
+    ap.add_argument("--fanout", choices=["off", "auto", "on"], default="off",
+                    help="N > 1, push: DP-replica fan-out (suika_b200.fanout); the default workloads have no replicas")
     ap.add_argument("--direction", choices=["pull", "push"], default="push",
                     help="N > 1: target ranks read their pieces (pull) or source ranks write them (push)")
     args = ap.parse_args()

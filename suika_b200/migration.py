@@ -676,6 +676,8 @@ class _Phased:
 
     def launch(self, stream: Optional[torch.cuda.Stream] = None) -> L.RsLaunchInfo:
         """Queue every phase of this rank back to back (asynchronous); no cross-rank pacing."""
+        if getattr(self, "_paced", False):
+            raise RuntimeError("a fan-out transfer reads in stage 2 what stage 1 wrote: use run()")
         info = L.RsLaunchInfo()
         for p in getattr(self, "prepared_phases", []):
             if p is not None:
@@ -866,6 +868,42 @@ def _push_table(prog: Program, rank: int, src_addr: Callable[[str, str], Tuple[i
     return out[: n.value]
 
 
+def _push_rank_tables(plan: Plan, rank: int, spec, subs: Sequence[str], src_addr: Callable[[str, str], Tuple[int, int]],
+                      arena_base: Callable[[int], int], slot_off: Callable[[int], np.ndarray], slot_nb: Callable[[int], np.ndarray],
+                      my_prog: Optional["Program"] = None, fanout=None):
+    """What `rank` writes in a push reshard. Stage 1: the pieces it is the source of, for every
+    target rank T (into arena_base(T) + slot_off(T)[slot]), minus the tensors T takes from a
+    fan-out leader. Stage 2 (fan-out only): the assembled tensors it forwards as a leader.
+    Returns (stage-1 table, target rank of each entry, {(follower, round): stage-2 table})."""
+    from .fanout import forward_table, stage1_keep
+    ops = plan.op_array
+    tables, peers_of = [], []
+    progs: Dict[int, Program] = {}
+
+    def prog_of(t: int) -> "Program":
+        if t == rank and my_prog is not None:
+            return my_prog
+        if t not in progs:
+            progs[t] = plan.program(t, spec)
+        return progs[t]
+
+    for T in sorted(set(int(t) for t in ops["dst_rank"][ops["src_rank"] == rank])):
+        prog = prog_of(T)
+        d = _push_table(prog, rank, src_addr, arena_base(T), slot_off(T), slot_nb(T), subs)
+        if fanout is not None and fanout.active:
+            d = d[stage1_keep(prog, rank, fanout.forwarded_names(T))]
+        tables.append(d)
+        peers_of.append(np.full(len(d), T, np.int64))
+    stage2: Dict[Tuple[int, int], np.ndarray] = {}
+    if fanout is not None and fanout.active:
+        for (F, rnd), names in fanout.children_of(rank).items():
+            stage2[(F, rnd)] = forward_table(prog_of(rank), arena_base(rank), slot_off(rank), prog_of(F), arena_base(F),
+                                             slot_off(F), slot_nb(F), names)
+    table = np.concatenate(tables) if tables else np.zeros(0, dtype=L.COPY_DESC_DTYPE)
+    peer = np.concatenate(peers_of) if peers_of else np.zeros(0, np.int64)
+    return table, peer, stage2
+
+
 class RankTransferPush(_Phased):
     """One rank's share of a reshard with targets written by their sources (same contract as
     RankTransfer: prepare / launch / finish, same targets byte for byte).
@@ -879,11 +917,16 @@ class RankTransferPush(_Phased):
     HBM over NVLink (posted writes, no read requests on the reverse direction).
     finish: after this rank's kernel has finished, a barrier; past it every rank's pieces have
     landed, and the arena mappings are closed.
+    fanout: a suika_b200.fanout.FanOut (plan_fanout of this plan, the same on every rank): stage
+    1 sends a replicated tensor to its leader only, stage 2 has leaders forward it to the other
+    replicas; run() paces the stages (launch() refuses).
     """
 
     def __init__(self, plan: Plan, source_state_dict: Dict[str, Dict[str, torch.Tensor]], expected_sub_fields,
                  device: torch.device, world: Optional[dist.ProcessGroup] = None, log_func: Optional[Callable] = None,
-                 phased: bool = True):
+                 phased: bool = True, fanout=None):
+        if fanout is not None and fanout.active and not phased:
+            raise ValueError("fan-out runs in phases (stage 2 reads what stage 1 wrote)")
         self.plan, self.device, self.world = plan, device, world
         self.source_state_dict = source_state_dict
         self.log = log_func or (lambda m: None)
@@ -936,9 +979,8 @@ class RankTransferPush(_Phased):
         dist.all_gather_object(g2, {"arena": arena_handle, "arena_offset": arena_offset, "off": slot_off, "nb": slot_nb},
                                group=world)
         try:
-            # 3. the pieces this rank sources, for every target rank
-            tables, peers_of = [], []
-            targets = sorted(set(int(t) for t in ops["dst_rank"][ops["src_rank"] == rank]))
+            # 3. the pieces this rank sources, for every target rank (and, with fan-out, the
+            # tensors it forwards as a leader)
             def src_addr(name, sub):
                 if name not in source_state_dict:
                     raise AssertionError(f"[{rank}]: param missing in source {name}")
@@ -946,17 +988,15 @@ class RankTransferPush(_Phased):
                 source_state_dict[name][sub] = v
                 return v.data_ptr(), v.numel() * v.element_size()
 
-            for T in targets:
-                prog = my_prog if T == rank else plan.program(T, spec)
-                base = self.arena.data_ptr() if T == rank else self.peers.base(T, 0, g2[T]["arena"]) + g2[T]["arena_offset"]
-                d = _push_table(prog, rank, src_addr, base, g2[T]["off"], g2[T]["nb"], subs)
-                nbytes = int((d["rows"] * d["row_bytes"]).sum())
-                if T == rank:
-                    self.local_bytes += nbytes
-                else:
-                    self.remote_bytes += nbytes
-                tables.append(d)
-                peers_of.append(np.full(len(d), T, np.int64))
+            def arena_base(T):
+                return self.arena.data_ptr() if T == rank else self.peers.base(T, 0, g2[T]["arena"]) + g2[T]["arena_offset"]
+
+            t1, peer1, stage2 = _push_rank_tables(plan, rank, spec, subs, src_addr, arena_base, lambda T: g2[T]["off"],
+                                                  lambda T: g2[T]["nb"], my_prog, fanout)
+            nb1 = (t1["rows"] * t1["row_bytes"]).astype(np.int64)
+            self.local_bytes += int(nb1[peer1 == rank].sum())
+            self.remote_bytes += int(nb1[peer1 != rank].sum()) + sum(int((d["rows"] * d["row_bytes"]).sum()) for d in stage2.values())
+            tables, peers_of = [t1], [peer1]
             # 4. this rank's targets: dict in the reference's order, singleton values staged locally
             if my_prog is not None:
                 ent: Dict[str, Dict[str, torch.Tensor]] = {}
@@ -981,10 +1021,25 @@ class RankTransferPush(_Phased):
                                for n in _name_order(plan, rank)}
             self.table = np.concatenate(tables) if tables else np.zeros(0, dtype=L.COPY_DESC_DTYPE)
             peer = np.concatenate(peers_of) if peers_of else np.zeros(0, np.int64)
-            self._stage_phases(self.table, peer, as_source=True, phased=phased)
+            if fanout is not None and fanout.active:
+                self._stage_fanout(self.table, peer, stage2, fanout)
+            else:
+                self._stage_phases(self.table, peer, as_source=True, phased=phased)
         except BaseException:
             self.peers.close()
             raise
+
+    def _stage_fanout(self, table: np.ndarray, peer: np.ndarray, stage2: Dict[Tuple[int, int], np.ndarray], fanout) -> None:
+        """Stage-1 phases (the plan's pairs without forwarded tensors), then stage-2 phases."""
+        t1 = _phase_tables(table, peer, self.rank, fanout.phase1, fanout.n1, as_source=True)
+        t2: List[List[np.ndarray]] = [[] for _ in range(fanout.n2)]
+        for (F, rnd), d in stage2.items():
+            t2[fanout.phase2[(self.rank, F, rnd)]].append(d)
+        tables = t1 + [np.concatenate(x) if x else np.zeros(0, dtype=L.COPY_DESC_DTYPE) for x in t2]
+        self.phase_of_pair, self.n_phases = dict(fanout.phase1), fanout.n_phases
+        self.prepared_phases = [PreparedCopies(t, self.device) if len(t) else None for t in tables]
+        self.prepared = None
+        self._paced = True
 
     def finish(self) -> Dict[str, Dict[str, torch.Tensor]]:
         """Wait for this rank's kernel, then for every rank (barrier): all pieces have landed."""
@@ -1007,12 +1062,23 @@ class RankTransferPush(_Phased):
 def execute_plan_distributed(plan: Plan, source_state_dict: Dict[str, Dict[str, torch.Tensor]], expected_sub_fields,
                              device: torch.device, world: Optional[dist.ProcessGroup] = None,
                              log_func: Optional[Callable] = None, timers: Optional[dict] = None, direction: str = "pull",
-                             phased: bool = True):
+                             phased: bool = True, fanout=False):
     """Run one rank's share of a reshard (execute_param_transfer, migration.py:397-556): prepare,
     one kernel launch, finish. Collective over `world`. direction="pull": each target rank reads
-    its pieces (RankTransfer); "push": each source rank writes them (RankTransferPush)."""
-    cls = {"pull": RankTransfer, "push": RankTransferPush}[direction]
-    rt = cls(plan, source_state_dict, expected_sub_fields, device, world, log_func, phased=phased)
+    its pieces (RankTransfer); "push": each source rank writes them (RankTransferPush).
+    fanout (push only): False, True or "auto", as suika_b200.fanout.plan_fanout takes it."""
+    if direction == "push":
+        fo = None
+        if fanout:
+            from .fanout import plan_fanout
+            fo = plan_fanout(plan, 1, mode=fanout)
+        rt = RankTransferPush(plan, source_state_dict, expected_sub_fields, device, world, log_func, phased=phased, fanout=fo)
+    elif direction == "pull":
+        if fanout:
+            raise ValueError("fan-out is implemented for the push direction")
+        rt = RankTransfer(plan, source_state_dict, expected_sub_fields, device, world, log_func, phased=phased)
+    else:
+        raise ValueError(f"direction {direction!r}: 'pull' or 'push'")
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record()
     rt.run()
@@ -1039,6 +1105,8 @@ def schedule_and_execute_param_transfer(source_param_layout, target_param_layout
     its pieces into the target ranks' memory (targets of a rank are views of one arena); "pull" has
     every target rank read them (targets are separate allocations). Transfers run in phases in
     which every GPU sends to at most one peer and receives from at most one.
+    $SUIKA_RESHARD_FANOUT ("0" by default, "auto" or "1"): DP-replica fan-out of the push
+    direction (suika_b200.fanout).
     """
     if not isinstance(device, torch.device):
         device = torch.device(device)
@@ -1055,8 +1123,9 @@ def schedule_and_execute_param_transfer(source_param_layout, target_param_layout
         # sources received in place from the old process (suika_b200.handoff) are memory another
         # process owns: they cannot be re-exported to peers, so this rank's own kernel reads them
         direction = "push"
+    fanout = {"0": False, "": False, "auto": "auto", "1": True}[os.environ.get("SUIKA_RESHARD_FANOUT", "0").strip().lower()]
     target = execute_plan_distributed(plan, source_state_dict, other_context_dict["expected_sub_fields"], device, world, log_func,
-                                      direction=direction)
+                                      direction=direction, fanout=fanout if direction == "push" else False)
     torch.cuda.synchronize(device=device)
     if callable(release):
         release()  # every rank is past the barrier: the old process may free its memory

@@ -1,11 +1,13 @@
 """The push direction's copy tables, executed on the CPU against emulated memory: every rank's
-table (the pieces it sources, for every target rank) applied to numpy buffers must rebuild the
-reference's targets (tests/golden digests). Covers the table logic of RankTransferPush without
-GPUs or IPC."""
+tables (built by the same function RankTransferPush uses) applied to numpy buffers must rebuild
+the reference's targets (tests/golden digests). Covers the table logic of RankTransferPush without
+GPUs or IPC, with and without DP-replica fan-out (suika_b200/fanout.py): with fan-out, stage 1
+runs first, then stage 2's phases in order, each phase a matching."""
 import numpy as np
 import pytest
 
 from suika_b200 import migration as M
+from suika_b200.fanout import plan_fanout
 from tests.golden.cases import CASES
 from tests.helpers import SUB_ITEMSIZE, SUBS, Memory, digest, golden_states, load_golden
 
@@ -13,12 +15,20 @@ SPEC = [(SUB_ITEMSIZE[s], kind == "meta") for s, kind in SUBS]
 SUBNAMES = [s for s, _ in SUBS]
 
 
-def run_push(case):
+def _apply(mem: Memory, table: np.ndarray) -> None:
+    for d in table:
+        rb = int(d["row_bytes"])
+        for row in range(int(d["rows"])):
+            mem.view(int(d["dst_dev"]) + row * int(d["dst_pitch"]), rb)[:] = mem.view(int(d["src_dev"]) + row * int(d["src_pitch"]), rb)
+
+
+def run_push(case, fanout=False):
     g = load_golden(case)
     cfg = CASES[case]["config"]
     spl, tpl = cfg.layouts()
     states = golden_states(cfg, seed=g["seed"])
     plan = M.Plan(spl, tpl, minimum_est_peers=g["minimum_est_peers"])
+    fo = plan_fanout(plan, 1, mode=True) if fanout else None
     mem = Memory()
     src_addr = {}
     for r, st in states.items():
@@ -35,20 +45,26 @@ def run_push(case):
         arr = np.full(max(total, 1), 0xAB, dtype=np.uint8)
         arenas[T] = (mem.add(arr), off, nb)
     ops = plan.op_array
-    for rank in sorted(set(int(x) for x in ops["src_rank"])):
-        for T in sorted(set(int(t) for t in ops["dst_rank"][ops["src_rank"] == rank])):
-            base, off, nb = arenas[T]
-            table = M._push_table(progs[T], rank, lambda n, s, r=rank: src_addr[(r, n, s)], base, off, nb, SUBNAMES)
-            for d in table:
-                for row in range(int(d["rows"])):
-                    rb = int(d["row_bytes"])
-                    mem.view(int(d["dst_dev"]) + row * int(d["dst_pitch"]), rb)[:] = mem.view(int(d["src_dev"]) + row * int(d["src_pitch"]), rb)
-    return g, plan, progs, arenas, mem
+    stage2 = []
+    for rank in sorted(set(int(x) for x in ops["src_rank"]) | set(arenas)):
+        t1, peer, s2 = M._push_rank_tables(plan, rank, SPEC, SUBNAMES, lambda n, s, r=rank: src_addr[(r, n, s)],
+                                           lambda T: arenas[T][0], lambda T: arenas[T][1], lambda T: arenas[T][2],
+                                           progs.get(rank), fo)
+        _apply(mem, t1)
+        for (F, rnd), d in s2.items():
+            stage2.append((fo.phase2[(rank, F, rnd)], rank, F, d))
+    if fo is not None:
+        for k in range(fo.n2):  # phases in order: a later round reads what an earlier one wrote
+            in_phase = [(s, f) for p, s, f, _ in stage2 if p == k]
+            assert len({s for s, _ in in_phase}) == len(in_phase) and len({f for _, f in in_phase}) == len(in_phase), in_phase
+            for p, _s, _f, d in stage2:
+                if p == k:
+                    _apply(mem, d)
+    return g, plan, progs, arenas, mem, fo
 
 
-@pytest.mark.parametrize("case", ["odd_mini", "cfg2b_mini", "cfg3_mini", "cfg4_mini", "shrink_mini", "hetero_mini"])
-def test_push_tables_rebuild_reference_targets(case):
-    g, plan, progs, arenas, mem = run_push(case)
+def _check(case, fanout):
+    g, plan, progs, arenas, mem, fo = run_push(case, fanout)
     for rank_s, want in g["ranks"].items():
         T = int(rank_s)
         base, off, nb = arenas[T]
@@ -60,3 +76,16 @@ def test_push_tables_rebuild_reference_targets(case):
                 if sub == "step":
                     continue
                 assert digest(got[(name, sub)]) == sha, (rank_s, name, sub)
+    return fo
+
+
+@pytest.mark.parametrize("case", ["odd_mini", "cfg2b_mini", "cfg3_mini", "cfg4_mini", "shrink_mini", "hetero_mini"])
+def test_push_tables_rebuild_reference_targets(case):
+    _check(case, fanout=False)
+
+
+@pytest.mark.parametrize("case", ["cfg2_mini", "cfg4_mini", "cfg5_mini", "hetero_mini", "shrink_mini"])
+def test_fanout_tables_rebuild_reference_targets(case):
+    """Forced fan-out (every exact replica forwarded): still the reference's bytes everywhere."""
+    fo = _check(case, fanout=True)
+    assert fo.active and fo.n2 >= 1
