@@ -43,6 +43,18 @@ def schedule_as_lists(ops):
     return [[o.name, o.src, o.dst, list(o.src_tp) if o.src_tp else None, list(o.dst_tp) if o.dst_tp else None] for o in ops]
 
 
+def copy_rect(dst: np.ndarray, do: int, dpitch: int, src: np.ndarray, so: int, spitch: int, rows: int, rb: int) -> None:
+    """rows x rb bytes from src[so + r * spitch] to dst[do + r * dpitch] (uint8 arrays), in one numpy
+    strided copy; both extents are checked first."""
+    if rows <= 0 or rb <= 0:
+        return
+    span_s, span_d = (rows - 1) * spitch + rb, (rows - 1) * dpitch + rb
+    assert so + span_s <= src.size and do + span_d <= dst.size, "rectangle leaves its buffer"
+    s = np.lib.stride_tricks.as_strided(src[so:so + span_s], shape=(rows, rb), strides=(spitch, 1))
+    d = np.lib.stride_tricks.as_strided(dst[do:do + span_d], shape=(rows, rb), strides=(dpitch, 1), writeable=True)
+    d[...] = s
+
+
 def emulate_program(prog, names, states, rank) -> Dict[str, Dict[str, np.ndarray]]:
     """Apply a Program's slots and segments with numpy; returns {name: {sub: array}}."""
     src_buf = []
@@ -55,11 +67,8 @@ def emulate_program(prog, names, states, rank) -> Dict[str, Dict[str, np.ndarray
         src_buf.append(b)
     dst_buf = [np.zeros(int(ds["nbytes"]), dtype=np.uint8) for ds in prog.dst_slots]
     for sg in prog.segments:
-        s, d = src_buf[sg["src_slot"]], dst_buf[sg["dst_slot"]]
-        rows, rb = int(sg["rows"]), int(sg["row_bytes"])
-        for r in range(rows):
-            so, do = int(sg["src_offset"]) + r * int(sg["src_pitch"]), int(sg["dst_offset"]) + r * int(sg["dst_pitch"])
-            d[do:do + rb] = s[so:so + rb]
+        copy_rect(dst_buf[sg["dst_slot"]], int(sg["dst_offset"]), int(sg["dst_pitch"]),
+                  src_buf[sg["src_slot"]], int(sg["src_offset"]), int(sg["src_pitch"]), int(sg["rows"]), int(sg["row_bytes"]))
     out: Dict[str, Dict[str, np.ndarray]] = {}
     for ds, buf in zip(prog.dst_slots, dst_buf):
         name = names[ds["name_id"]]
@@ -93,3 +102,14 @@ class Memory:
             if base <= addr and addr + n <= base + a.nbytes:
                 return a[addr - base: addr - base + n]
         raise AssertionError(f"address {addr:#x}+{n} outside every buffer")
+
+    def apply(self, descs: np.ndarray) -> None:
+        """Run COPY_DESC entries against this memory."""
+        for d in descs:
+            rows, rb = int(d["rows"]), int(d["row_bytes"])
+            if rows <= 0 or rb <= 0:
+                continue
+            sp, dp = int(d["src_pitch"]), int(d["dst_pitch"])
+            s = self.view(int(d["src_dev"]), (rows - 1) * sp + rb)
+            t = self.view(int(d["dst_dev"]), (rows - 1) * dp + rb)
+            copy_rect(t, 0, dp, s, 0, sp, rows, rb)

@@ -31,11 +31,7 @@ def _slice_size(case):
 
 
 def _apply(mem: Memory, descs: np.ndarray) -> None:
-    for d in descs:
-        rb = int(d["row_bytes"])
-        for row in range(int(d["rows"])):
-            mem.view(int(d["dst_dev"]) + row * int(d["dst_pitch"]), rb)[:] = \
-                mem.view(int(d["src_dev"]) + row * int(d["src_pitch"]), rb)
+    mem.apply(descs)
 
 
 def test_golden_covers_every_case():

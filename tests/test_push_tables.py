@@ -16,10 +16,7 @@ SUBNAMES = [s for s, _ in SUBS]
 
 
 def _apply(mem: Memory, table: np.ndarray) -> None:
-    for d in table:
-        rb = int(d["row_bytes"])
-        for row in range(int(d["rows"])):
-            mem.view(int(d["dst_dev"]) + row * int(d["dst_pitch"]), rb)[:] = mem.view(int(d["src_dev"]) + row * int(d["src_pitch"]), rb)
+    mem.apply(table)
 
 
 def run_push(case, fanout=False):
