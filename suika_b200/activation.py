@@ -203,6 +203,10 @@ class ActivationExchange:
         src_bsz, dst_bsz = self.src.rank_bsz(), self.dst.rank_bsz()
         if set(src_bsz) & set(dst_bsz):
             raise AssertionError("the two stages share ranks")
+        members = set(dist.get_process_group_ranks(group)) if group is not None else set(range(dist.get_world_size()))
+        missing = (set(src_bsz) | set(dst_bsz)) - members
+        if missing:
+            raise AssertionError(f"ranks {sorted(missing)} of the two stages are not in the exchange's process group")
         self.is_sender, self.is_receiver = self.rank in src_bsz, self.rank in dst_bsz
         self.my_src_shape = _local_shape(self.shape, self.bd, src_bsz.get(self.rank, 0))
         self.my_dst_shape = _local_shape(self.shape, self.bd, dst_bsz.get(self.rank, 0))

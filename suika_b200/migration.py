@@ -1091,6 +1091,15 @@ def execute_plan_distributed(plan: Plan, source_state_dict: Dict[str, Dict[str, 
     return target
 
 
+def _fanout_setting(value: str):
+    """$SUIKA_RESHARD_FANOUT: "0" / "" (off), "auto", "1" (wherever exact)."""
+    v = value.strip().lower()
+    table = {"0": False, "": False, "off": False, "auto": "auto", "1": True, "on": True}
+    if v not in table:
+        raise ValueError(f"SUIKA_RESHARD_FANOUT={value!r}: use 0, auto or 1")
+    return table[v]
+
+
 def schedule_and_execute_param_transfer(source_param_layout, target_param_layout, source_state_dict: Dict[str, Dict[str, torch.Tensor]],
                                         other_context_dict: Dict[str, Any], device, world: Optional[dist.ProcessGroup],
                                         prof=None, forcefully_free: bool = False, log_func=None, direction: Optional[str] = None):
@@ -1123,7 +1132,7 @@ def schedule_and_execute_param_transfer(source_param_layout, target_param_layout
         # sources received in place from the old process (suika_b200.handoff) are memory another
         # process owns: they cannot be re-exported to peers, so this rank's own kernel reads them
         direction = "push"
-    fanout = {"0": False, "": False, "auto": "auto", "1": True}[os.environ.get("SUIKA_RESHARD_FANOUT", "0").strip().lower()]
+    fanout = _fanout_setting(os.environ.get("SUIKA_RESHARD_FANOUT", "0"))
     target = execute_plan_distributed(plan, source_state_dict, other_context_dict["expected_sub_fields"], device, world, log_func,
                                       direction=direction, fanout=fanout if direction == "push" else False)
     torch.cuda.synchronize(device=device)

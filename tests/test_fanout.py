@@ -1,6 +1,6 @@
 """DP-replica fan-out planning (suika_b200/fanout.py), on the CPU: where it applies and what its
-cost model decides, the broadcast trees' shape, and a DP grow x8 run through the push tables on
-emulated memory against the oracle."""
+cost model decides, the broadcast trees' shape, the switch of the drop-in, and a DP grow x4 run
+through the push tables on emulated memory against the oracle."""
 import math
 
 import numpy as np
@@ -11,7 +11,7 @@ from suika_b200 import migration as M
 from suika_b200 import synthetic as S
 from suika_b200.fanout import plan_fanout
 from suika_b200.layouts import CONFIGS, SPECS, ReshardConfig, scaled_spec
-from tests.helpers import SUB_ITEMSIZE, SUB_META, SUBS, Memory
+from tests.helpers import SUB_META, SUBS, Memory
 from tests.test_push_tables import SPEC, SUBNAMES, _apply
 
 STATE_BYTES = 14  # bf16 param + fp32 master, m, v per element
@@ -103,3 +103,10 @@ def test_dp_grow_tables_with_fanout_match_the_oracle(order):
                 continue
             got = mem.view(base + int(o), int(n))
             assert np.array_equal(got, want[name][sub].reshape(-1).view(np.uint8)), (T, name, sub)
+
+
+def test_fanout_switch_values():
+    assert M._fanout_setting("0") is False and M._fanout_setting("") is False
+    assert M._fanout_setting(" AUTO ") == "auto" and M._fanout_setting("1") is True
+    with pytest.raises(ValueError, match="SUIKA_RESHARD_FANOUT"):
+        M._fanout_setting("yes")
