@@ -11,6 +11,11 @@ Workloads (synthetic seeded state, BASELINE sub-fields: bf16 param + fp32 master
          is one launch of each rank's pull kernel (peer HBM over NVLink + own HBM).
 `value` is the state moved by all ranks per second (GB/s, bytes that must be written into
 target tensors); the time of a step is the max over ranks of the device time.
+
+Other modes (not the driver's contract lines): --impl reference-nccl (the reference's own GPU
+path, execute_param_transfer over NCCL, on the N > 1 workload), --handoff (old -> new process
+hand-off, 1 GPU), --activation (pipeline activation hand-over, N >= 2), --metadata (layout
+exchange and planning, any N; gloo without GPUs), --fanout (DP-replica fan-out of the push path).
 """
 from __future__ import annotations
 
@@ -440,6 +445,61 @@ def run_dist(args):
     return res
 
 
+def run_reference_nccl(args):
+    """The reference's own GPU data path on run_dist's workload: oracle/nccl_port.py restates
+    execute_param_transfer (Suika/migration.py:397-556) with one NCCL isend/irecv per tensor and
+    sub-field, .contiguous() chunks, then cat / clone and cuda_gc. A step is one execute on every
+    rank from a fresh shallow copy of the source dict (the reference clears it); device time from
+    before the first op to after the last cat, max over ranks."""
+    from oracle import nccl_port as P
+    from oracle import restate as O
+    rank, world = dist.get_rank(), dist.get_world_size()
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    dev = torch.device("cuda", local)
+    cfg = workload(world, args.layers)
+    spl, tpl = cfg.layouts()
+    state = S.DeviceState(spl.layout[rank], dev)
+    torch.cuda.synchronize()
+    ops = O.schedule(spl, tpl, minimum_est_peers=1)
+    subfields = [(s, k == "meta", S.TORCH_DTYPE[k]) for s, k in S.SUBFIELDS]
+    shapes = {n: m.shape for metas in tpl.layout.values() for n, m in metas.items()}
+    plan = M.Plan(spl, tpl, minimum_est_peers=1)
+    its = [2, 4, 4, 4]
+    rb = plan.rank_bytes(its)
+    moved_all = int(plan.op_array["numel"].sum()) * sum(its)
+    times = []
+    with Clocks(local) as ck:
+        for i in range(args.warmup + args.steps):
+            src = {n: dict(e) for n, e in state.state.items()}
+            dist.barrier()
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            out = P.execute_rank(ops, src, subfields, shapes, rank, dev)
+            b.record()
+            torch.cuda.synchronize()
+            if i >= args.warmup:
+                times.append(a.elapsed_time(b))
+            del out
+    per_rank = [None] * world
+    dist.all_gather_object(per_rank, round(statistics.mean(times), 4))
+    t = max(per_rank) / 1e3
+    if rank != 0:
+        return None
+    max_dir = max(max(rb["ingress"].values(), default=0), max(rb["egress"].values(), default=0))
+    return {
+        "metric": METRIC, "impl": "reference-nccl", "value": round(moved_all / t / 1e9, 2), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t * 1e3, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic (as the ours arm)",
+        "config": {"workload": f"{cfg.name}: {cfg.note}, full training state (bf16 param + fp32 master/m/v + step)",
+                   "path": "oracle/nccl_port.py: execute_param_transfer over NCCL P2P per tensor, cat/clone, cuda_gc"},
+        "migration_s": round(t, 6), "nvlink_gbs_per_gpu": round(max(rb["ingress"].values(), default=0) / t / 1e9, 2),
+        "roofline": {"bound": "nvlink", "achieved": round(max_dir / t / 1e9, 1), "peak": NVLINK_PEER_GBS, "unit": "GB/s",
+                     "frac": round(max_dir / t / 1e9 / NVLINK_PEER_GBS, 4)},
+        "per_rank_ms": per_rank, "clocks": ck.summary(),
+    }
+
+
 def region_checksum(t: torch.Tensor, offset: int, rows: int, row_bytes: int, pitch: int) -> int:
     """Position-weighted checksum (mod 2^64) of a strided byte region of tensor t's storage."""
     b = t.reshape(-1).view(torch.uint8) if t.dim() else t.reshape(1).view(torch.uint8)
@@ -563,7 +623,9 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--impl", choices=["ours", "reference", "reference-nccl"], default="ours",
+                    help="reference: the CPU oracle (the driver's reference arm); reference-nccl: the reference's "
+                         "own GPU path (execute_param_transfer over NCCL P2P per tensor, N > 1 under torchrun)")
     ap.add_argument("--layers", type=int, default=0, help="override the workload's layer count (smaller cases)")
     ap.add_argument("--e2e-layers", type=int, default=8)
     ap.add_argument("--e2e-steps", type=int, default=3)
@@ -619,13 +681,15 @@ def main():
         if rank == 0:
             print(json.dumps(run_reference(args, max(world, args.gpus))), flush=True)
         return
+    if args.impl == "reference-nccl" and world < 2:
+        raise SystemExit("--impl reference-nccl times the reference's P2P path: run N >= 2 ranks under torchrun")
     if world > 1:
         import datetime
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", rank)))
         os.environ.setdefault("NCCL_DEBUG", "WARN")  # keep stdout to the one JSON line
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
         try:
-            res = run_dist(args)
+            res = run_reference_nccl(args) if args.impl == "reference-nccl" else run_dist(args)
         finally:
             dist.barrier()
             dist.destroy_process_group()
