@@ -3,7 +3,7 @@
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
   (N > 1: torchrun --nproc-per-node N bench.py --gpus N ...)
 
-Workloads (synthetic seeded state, BASELINE sub-fields: bf16 param + fp32 master/m/v + step):
+Workloads (synthetic seeded state, sub-fields bf16 param + fp32 master/m/v + step):
   N = 1  cfg2b: Llama2-7B full state, TP1 -> TP2 on one GPU, dim-0 slices and replicated tensors
          as views, row-split (dim -1) pieces packed; a step is one launch of the pack kernel.
   N > 1  Llama2-13B-shaped, 5*N layers, TP N x PP1 -> TP N/2 x PP2 (N = 8 is cfg3 exactly:

@@ -1,5 +1,5 @@
 """The reference's execute_param_transfer as it runs on GPUs: one torch.distributed P2P op per
-tensor and sub-field (TEST AND BASELINE INFRASTRUCTURE ONLY; see oracle/__init__.py).
+tensor and sub-field (TEST AND BENCHMARK-BASELINE INFRASTRUCTURE ONLY; see oracle/__init__.py).
 
 Restates Suika/migration.py:397-556, with the P2P helper of Suika/utils.py:212-234 (non-batched
 isend/irecv, issued in op order), on torch tensors:

@@ -19,7 +19,7 @@ per tensor). Here:
     process exits) is copied on receipt, as the reference does, and acknowledged at once: one copy
     of the whole arena, the received tensors being views of it.
 
-Both processes must use these two functions (rebind them in Suika.migration, see INTEGRATION.md).
+Both processes must use these two functions (rebind them in Suika.migration).
 """
 from __future__ import annotations
 

@@ -1,6 +1,6 @@
 """Seeded synthetic training state for reshard parity tests and benchmarks.
 
-State per tensor (the BASELINE sub-fields, in this order):
+State per tensor (the benchmark's sub-fields, in this order):
     param       bf16   = round-to-nearest-even of master
     step        fp32   singleton (Adam step; a "meta" sub-field, migration.py:702-709)
     master      fp32   weights and biases ~ N(0, 0.02); norm weights 1.0, norm biases 0.0

@@ -1,8 +1,8 @@
 """Parity cases shared by the golden generator and the tests.
 
-Full-width BASELINE shapes are too large for a CPU run of the reference, so most cases keep the
+Full-width benchmark shapes are too large for a CPU run of the reference, so most cases keep the
 reference's tensor names, module order and slicing at reduced widths and depths; cfg1 runs at its
-full size. Each case names the reshard (meshes) of the BASELINE configuration it stands for.
+full size. Each case names the reshard (meshes) of the benchmark configuration it stands for.
 """
 from suika_b200.layouts import CONFIGS, SPECS, ReshardConfig, scaled_spec
 

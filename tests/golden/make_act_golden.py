@@ -1,6 +1,6 @@
 """Generate tests/golden/act_golden.json by running Suika's own activation-exchange generator.
 
-Run in a checkout that has the reference (read-only) at $SUIKA_REFERENCE (default /root/reference):
+Run where the reference checkout (read-only) is importable; $SUIKA_REFERENCE names its directory:
 
     python tests/golden/make_act_golden.py
 
@@ -79,7 +79,9 @@ def run_case(case: dict, P, RawDeviceMesh2D, dist) -> dict:
 
 
 def main() -> None:
-    ref = os.environ.get("SUIKA_REFERENCE", "/root/reference")
+    ref = os.environ.get("SUIKA_REFERENCE")
+    if not ref:
+        raise SystemExit("set SUIKA_REFERENCE to the directory of the reference checkout (the one holding Suika/)")
     sys.path.insert(0, ref)
     import torch.distributed as dist
     dist.init_process_group("gloo", init_method="tcp://127.0.0.1:29631", rank=0, world_size=1)

@@ -1,6 +1,6 @@
 """Generate golden digests by running Suika's own reshard code on CPU/gloo ranks.
 
-Run in a checkout that has the reference (read-only) at $SUIKA_REFERENCE (default /root/reference):
+Run where the reference checkout (read-only) is importable; $SUIKA_REFERENCE names its directory:
 
     python tests/golden/make_golden.py [case ...]
 
@@ -99,7 +99,9 @@ def run_case(name: str, port: int) -> dict:
     case = CASES[name]
     cfg = case["config"]
     world = cfg.world_size
-    ref = os.environ.get("SUIKA_REFERENCE", "/root/reference")
+    ref = os.environ.get("SUIKA_REFERENCE")
+    if not ref:
+        raise SystemExit("set SUIKA_REFERENCE to the directory of the reference checkout (the one holding Suika/)")
     results = {}
     with tempfile.TemporaryDirectory() as outdir:
         mp.spawn(_worker, args=(world, name, port, ref, outdir), nprocs=world, join=True)
