@@ -60,7 +60,16 @@ def peaks():
 # ---------------------------------------------------------------------------------------------
 # Workloads
 # ---------------------------------------------------------------------------------------------
-def workload(n_gpus: int, layers: int = 0) -> ReshardConfig:
+def workload(n_gpus: int, layers: int = 0, config: str = "") -> ReshardConfig:
+    """The reshard a run of n_gpus ranks measures: cfg2b at N = 1, the Llama2-13B TP N -> TP N/2 x
+    PP2 family at N > 1 (cfg3 at N = 8), or a named configuration whose rank count is N."""
+    if config:
+        cfg = CONFIGS[config]
+        if cfg.world_size != n_gpus:
+            raise SystemExit(f"{config} runs on {cfg.world_size} ranks, not {n_gpus}")
+        if layers:
+            cfg = ReshardConfig(cfg.name, scaled_spec(cfg.spec, n_layers=layers), cfg.src_mesh, cfg.dst_mesh, cfg.note)
+        return cfg
     if n_gpus == 1:
         cfg = CONFIGS["cfg2b"]
         if layers:
@@ -366,9 +375,9 @@ def run_dist(args):
     rank, world = dist.get_rank(), dist.get_world_size()
     local = int(os.environ.get("LOCAL_RANK", rank))
     dev = torch.device("cuda", local)
-    cfg = workload(world, args.layers)
+    cfg = workload(world, args.layers, args.config)
     spl, tpl = cfg.layouts()
-    state = S.DeviceState(spl.layout[rank], dev)
+    state = S.DeviceState(spl.layout.get(rank, {}), dev)
     torch.cuda.synchronize()
     exp = S.expected_sub_fields()
     plan = M.Plan(spl, tpl, minimum_est_peers=1)
@@ -456,9 +465,9 @@ def run_reference_nccl(args):
     rank, world = dist.get_rank(), dist.get_world_size()
     local = int(os.environ.get("LOCAL_RANK", rank))
     dev = torch.device("cuda", local)
-    cfg = workload(world, args.layers)
+    cfg = workload(world, args.layers, args.config)
     spl, tpl = cfg.layouts()
-    state = S.DeviceState(spl.layout[rank], dev)
+    state = S.DeviceState(spl.layout.get(rank, {}), dev)
     torch.cuda.synchronize()
     ops = O.schedule(spl, tpl, minimum_est_peers=1)
     subfields = [(s, k == "meta", S.TORCH_DTYPE[k]) for s, k in S.SUBFIELDS]
@@ -551,9 +560,9 @@ def e2e_dist(args, world, rank, dev):
     """The drop-in schedule_and_execute_param_transfer end to end on a layer sample: per step the
     source shard is copied in from pinned host memory, the call plans, exchanges handles, maps
     peers, pulls and syncs, and the targets are read back to pinned host memory."""
-    cfg = workload(world, 2)  # one decoder layer per target stage keeps every rank's pinned buffers small
+    cfg = workload(world, 2, args.config)  # one decoder layer per target stage keeps every rank's pinned buffers small
     spl, tpl = cfg.layouts()
-    state = S.DeviceState(spl.layout[rank], dev)
+    state = S.DeviceState(spl.layout.get(rank, {}), dev)
     host = {k: torch.empty(a.shape, dtype=a.dtype, pin_memory=True) for k, a in state.arenas.items()}
     for k, a in state.arenas.items():
         host[k].copy_(a)
@@ -601,7 +610,7 @@ def e2e_dist(args, world, rank, dev):
 # Reference arm: the oracle port on the host cores (rank 0 only)
 # ---------------------------------------------------------------------------------------------
 def run_reference(args, world):
-    cfg = workload(world, args.layers)
+    cfg = workload(world, args.layers, args.config)
     threads = os.cpu_count() or 1
     smp = OracleSample(cfg, world, threads)
     for _ in range(args.warmup):
@@ -627,6 +636,8 @@ def main():
                     help="reference: the CPU oracle (the driver's reference arm); reference-nccl: the reference's "
                          "own GPU path (execute_param_transfer over NCCL P2P per tensor, N > 1 under torchrun)")
     ap.add_argument("--layers", type=int, default=0, help="override the workload's layer count (smaller cases)")
+    ap.add_argument("--config", default="", choices=["", "cfg1", "cfg2", "cfg3", "cfg4", "cfg5"],
+                    help="N > 1: measure this named reshard instead of the default family (its rank count must be N)")
     ap.add_argument("--e2e-layers", type=int, default=8)
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--e2e-warmup", type=int, default=1)
