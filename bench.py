@@ -36,7 +36,7 @@ sys.path.insert(0, REPO)
 
 from suika_b200 import migration as M  # noqa: E402
 from suika_b200 import synthetic as S  # noqa: E402
-from suika_b200.layouts import CONFIGS, SPECS, ReshardConfig, scaled_spec  # noqa: E402
+from suika_b200.layouts import CONFIGS, EXTRA_CONFIGS, SPECS, ReshardConfig, scaled_spec  # noqa: E402
 
 METRIC = "state-migration time (s) and NVLink GB/s per GPU for 3D-layout reshard"
 FALLBACK_HBM_GBS = 6650.0
@@ -64,7 +64,7 @@ def workload(n_gpus: int, layers: int = 0, config: str = "") -> ReshardConfig:
     """The reshard a run of n_gpus ranks measures: cfg2b at N = 1, the Llama2-13B TP N -> TP N/2 x
     PP2 family at N > 1 (cfg3 at N = 8), or a named configuration whose rank count is N."""
     if config:
-        cfg = CONFIGS[config]
+        cfg = CONFIGS.get(config) or EXTRA_CONFIGS[config]
         if cfg.world_size != n_gpus:
             raise SystemExit(f"{config} runs on {cfg.world_size} ranks, not {n_gpus}")
         if layers:
@@ -529,8 +529,8 @@ def verify_dist(plan, rt, rank, src_state, exp) -> dict:
     tensor (computed by the source rank on its own copy). Pieces land in their cat position by the
     same program the small-size parity tests pin against the reference."""
     subs = [s for s, _ in exp]
-    its = {s: t.element_size() for s, t in next(iter(src_state.values())).items() if t.dim() > 0}
-    spec = [(its[s], False) if s in its else (4, True) for s in subs]
+    kinds = dict(S.SUBFIELDS)  # a rank may hold no source (a DP grow's new ranks)
+    spec = [(4, True) if kinds[s] == "meta" else (S.TORCH_DTYPE[kinds[s]].itemsize, False) for s in subs]
     mine = []
     if rt.target:
         prog = plan.program(rank, spec)
@@ -636,8 +636,9 @@ def main():
                     help="reference: the CPU oracle (the driver's reference arm); reference-nccl: the reference's "
                          "own GPU path (execute_param_transfer over NCCL P2P per tensor, N > 1 under torchrun)")
     ap.add_argument("--layers", type=int, default=0, help="override the workload's layer count (smaller cases)")
-    ap.add_argument("--config", default="", choices=["", "cfg1", "cfg2", "cfg3", "cfg4", "cfg5"],
-                    help="N > 1: measure this named reshard instead of the default family (its rank count must be N)")
+    ap.add_argument("--config", default="", choices=["", "cfg1", "cfg2", "cfg3", "cfg4", "cfg5", "dpgrow8"],
+                    help="N > 1: measure this named reshard instead of the default family (its rank count must be N); "
+                         "dpgrow8 is the DP grow from one GPU to eight where --fanout applies")
     ap.add_argument("--e2e-layers", type=int, default=8)
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--e2e-warmup", type=int, default=1)

@@ -229,6 +229,7 @@ CONFIGS: Dict[str, ReshardConfig] = {
 }
 
 
+
 def shard_spans(full_shape: Sequence[int], tp_meta, rule=None) -> List[Tuple[int, int]]:
     """[lo, hi) intervals of the slice dim a shard holds, in storage order: the contiguous chunk
     of the reference, or, with a rule, each group's units (see rs_slice_rule in the C header)."""
@@ -265,3 +266,13 @@ def scaled_spec(spec: ModelSpec, **overrides) -> ModelSpec:
     d = dict(spec.__dict__)
     d.update(overrides)
     return ModelSpec(**d)
+
+
+# Reshards beyond the benchmark's list, for paths its configurations do not exercise.
+EXTRA_CONFIGS: Dict[str, ReshardConfig] = {
+    # DP grow from one GPU to eight: every target needs the whole state, which one GPU holds.
+    # Half of Llama2-7B's layers keep source plus target of rank 0 within one GPU's memory.
+    "dpgrow8": ReshardConfig("dpgrow8", scaled_spec(SPECS["llama2-7b"], name="llama2-7b-16L", n_layers=16), _m([[0]]),
+                             _m([[i] for i in range(8)]),
+                             "Llama2-7B-shaped 16 layers TP1xDP1 (1 GPU) -> TP1xDP8 (8 GPUs), the DP-replica fan-out case"),
+}

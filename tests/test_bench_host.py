@@ -22,6 +22,7 @@ def test_workloads():
         assert cfg.world_size == 8 and cfg.spec.n_layers == 2
     with pytest.raises(SystemExit, match="runs on 8 ranks"):
         bench.workload(4, 0, "cfg3")
+    assert bench.workload(8, 0, "dpgrow8").spec.n_layers == 16
 
 
 def test_activation_stages():
