@@ -1091,6 +1091,41 @@ def execute_plan_distributed(plan: Plan, source_state_dict: Dict[str, Dict[str, 
     return target
 
 
+def self_pieces(plan: Plan, source_state_dict: Dict[str, Dict[str, torch.Tensor]], expected_sub_fields, rank: int,
+                device: torch.device) -> List[torch.Tensor]:
+    """The tensors the reference's forcefully_free releases on `rank` (migration.py:539-541): a
+    self-transferred piece whose source TP degree is at least the target piece's is the source
+    tensor itself (get_send_tensor, migration.py:297-300), and a singleton's piece is the source
+    tensor when it already lives on `device` (tensor.to(device), :445-446)."""
+    ops = plan.op_array
+    m = (ops["src_rank"] == rank) & (ops["dst_rank"] == rank) & (ops["src_tp_deg"] >= ops["dst_tp_deg"])
+    out: List[torch.Tensor] = []
+    seen = set()
+    for nid in ops["name_id"][m]:
+        name = plan.names[int(nid)]
+        if name in seen or name not in source_state_dict:
+            continue
+        seen.add(name)
+        for sub, ft in expected_sub_fields:
+            t = source_state_dict[name].get(sub)
+            if not isinstance(t, torch.Tensor):
+                continue
+            if _is_meta_field(ft) and t.device != device:
+                continue  # the reference frees its device copy, not the host source
+            out.append(t)
+    return out
+
+
+def _forcefully_free(tensors: List[torch.Tensor]) -> None:
+    """forcefully_free_tensor (Suika/utils.py:255-260) on each tensor."""
+    for t in tensors:
+        st = t.untyped_storage()
+        if st.resizable():
+            st.resize_(0)
+        else:
+            t.data = torch.empty(0, device="meta")
+
+
 def _fanout_setting(value: str):
     """$SUIKA_RESHARD_FANOUT: "0" / "" (off), "auto", "1" (wherever exact)."""
     v = value.strip().lower()
@@ -1107,8 +1142,11 @@ def schedule_and_execute_param_transfer(source_param_layout, target_param_layout
 
     Same arguments, same return value ({name: {sub_field: tensor}} of this rank, tensors new and
     contiguous), same side effect (source_state_dict cleared). The targets are byte-identical to
-    the reference's, including its order of concatenated pieces. `forcefully_free` is accepted for
-    signature compatibility: no temporary piece tensors exist to free.
+    the reference's, including its order of concatenated pieces.
+
+    forcefully_free: as in the reference (migration.py:539-541), the storages of this rank's
+    self-sent pieces that are whole source tensors are released after the transfer (the shrink
+    path of migration_save passes True, so the old state is gone before the hand-off).
 
     direction (default: $SUIKA_RESHARD_DIRECTION, else "push"): "push" has every source rank write
     its pieces into the target ranks' memory (targets of a rank are views of one arena); "pull" has
@@ -1133,11 +1171,14 @@ def schedule_and_execute_param_transfer(source_param_layout, target_param_layout
         # process owns: they cannot be re-exported to peers, so this rank's own kernel reads them
         direction = "push"
     fanout = _fanout_setting(os.environ.get("SUIKA_RESHARD_FANOUT", "0"))
-    target = execute_plan_distributed(plan, source_state_dict, other_context_dict["expected_sub_fields"], device, world, log_func,
+    exp = other_context_dict["expected_sub_fields"]
+    to_free = self_pieces(plan, source_state_dict, exp, dist.get_rank(world), device) if forcefully_free else []
+    target = execute_plan_distributed(plan, source_state_dict, exp, device, world, log_func,
                                       direction=direction, fanout=fanout if direction == "push" else False)
     torch.cuda.synchronize(device=device)
     if callable(release):
         release()  # every rank is past the barrier: the old process may free its memory
+    _forcefully_free(to_free)  # past the barrier no rank reads them any more
     prof.stop("execute", require_memory=True)
     return target
 
@@ -1178,7 +1219,11 @@ def execute_param_transfer(transfer_ops: TransferSchedule, source_state_dict, de
     if fake_source_state_dicts is not None:
         r = dist.get_rank(world) if rank is None else rank
         return execute_from_host(transfer_ops.plan, r, source_state_dict, fake_source_state_dicts, expected_sub_fields, device)
-    return execute_plan_distributed(transfer_ops.plan, source_state_dict, expected_sub_fields, device, world, log_func)
+    to_free = self_pieces(transfer_ops.plan, source_state_dict, expected_sub_fields, dist.get_rank(world), device) if forcefully_free else []
+    target = execute_plan_distributed(transfer_ops.plan, source_state_dict, expected_sub_fields, device, world, log_func)
+    torch.cuda.synchronize(device=device)
+    _forcefully_free(to_free)
+    return target
 
 
 def execute_from_host(plan: Plan, rank: int, source_state_dict, fake_source_state_dicts, expected_sub_fields,
