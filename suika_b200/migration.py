@@ -91,8 +91,28 @@ class TensorMeta:
         s[self.slice_dim()] //= self.tp_deg()
         return torch.Size(s)
 
+    def scale_to_tp(self, target_tp_deg: int) -> List["TensorMeta"]:
+        """The pieces of this shard at a finer TP degree (migration.py:103-118); itself otherwise."""
+        if self.is_tp() and target_tp_deg > self.tp_deg():
+            d, i, g = self.tp_meta
+            k = target_tp_deg // g
+            return [TensorMeta(name=self.name, dtype=self.dtype, shape=self.shape, tp_meta=(d, k * i + j, target_tp_deg))
+                    for j in range(k)]
+        return [self]
+
+    def __eq__(self, other: Any) -> bool:
+        """migration.py:120-124: same TP-ness and slice dim, dtype and full shape."""
+        if not isinstance(other, TensorMeta):
+            return False
+        return (self.is_tp() == other.is_tp() and self.slice_dim() == other.slice_dim()
+                and self.dtype == other.dtype and torch.Size(self.shape) == torch.Size(other.shape))
+
+    __hash__ = None  # like the reference's class, which defines __eq__ only
+
     def __repr__(self) -> str:
         return f"TensorMeta(name={self.name}, {self.dtype}, {self.shape}, {self.tp_meta})"
+
+    __str__ = __repr__
 
 
 def get_named_parameters_and_persistent_buffers(model: torch.nn.Module):
@@ -124,8 +144,44 @@ class ParamLayout:
         for rank, m in enumerate(metas):
             self.layout[rank] = m
 
+    def is_owned(self, rank: int, param) -> bool:
+        """migration.py:195-205: the rank holds the tensor (by name), or a shard that owns the
+        given piece (by TensorMeta)."""
+        if isinstance(param, str):
+            return param in self.layout[rank]
+        name = param.name
+        return name in self.layout[rank] and self.is_tensor_tp_owned(self.layout[rank][name], param)
+
+    def owners(self, param) -> List[int]:
+        """migration.py:207-208."""
+        return [rank for rank in self.layout if self.is_owned(rank, param)]
+
+    @staticmethod
+    def is_tensor_tp_overlap(meta1, meta2) -> bool:
+        """migration.py:220-244 (the planner's C++ restates the same test)."""
+        a = meta1.tp_meta if hasattr(meta1, "tp_meta") else meta1
+        b = meta2.tp_meta if hasattr(meta2, "tp_meta") else meta2
+        if a is None or b is None:
+            return True
+        assert a[0] == b[0], f"slice dim mismatch {a[0]} vs {b[0]}"
+        (_, i1, g1), (_, i2, g2) = a, b
+        if g1 > g2:
+            i1, i2, g1, g2 = i2, i1, g2, g1
+        return i2 // (g2 // g1) == i1
+
+    @staticmethod
+    def is_tensor_tp_owned(meta_src, meta_tgt) -> bool:
+        """migration.py:246-254."""
+        a = meta_src.tp_meta if hasattr(meta_src, "tp_meta") else meta_src
+        b = meta_tgt.tp_meta if hasattr(meta_tgt, "tp_meta") else meta_tgt
+        da = a[2] if a is not None else 1
+        db = b[2] if b is not None else 1
+        return da <= db and ParamLayout.is_tensor_tp_overlap(a, b)
+
     def __repr__(self) -> str:
         return f"ParamLayout(\n  {self.layout}\n)"
+
+    __str__ = __repr__
 
 
 class TransferOp:
