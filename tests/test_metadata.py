@@ -104,3 +104,39 @@ def test_gather_and_broadcast_over_gloo_ranks():
             if p.is_alive():
                 p.kill()
     assert all(v == "ok" for v in res.values()), res
+
+
+def _dying_worker(rank, world, port, q):
+    import datetime
+    import time
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    if rank == 1:
+        os._exit(3)  # a rank that dies before the layout exchange
+    spl, _ = CONFIGS["cfg1"].layouts()
+    t0 = time.perf_counter()
+    try:
+        MD.gather_param_layout(spl.layout[rank])
+        q.put((rank, "no error"))
+    except Exception as e:
+        q.put((rank, f"raised {type(e).__name__} after {time.perf_counter() - t0:.1f}s"))
+
+
+def test_gather_fails_loudly_when_a_rank_dies():
+    """A rank that dies before the exchange makes the others' gather raise (gloo error or the
+    process group's 5 s timeout), never hang."""
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_dying_worker, args=(r, 2, 29719, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    try:
+        rank, msg = q.get(timeout=120)
+    finally:
+        for p in procs:
+            p.join(30)
+            if p.is_alive():
+                p.kill()
+    assert rank == 0 and msg.startswith("raised"), msg
