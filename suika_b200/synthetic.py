@@ -99,6 +99,7 @@ def host_states(layout, subfields=SUBFIELDS, seed: int = 0, distinct_steps: bool
     from concurrent.futures import ThreadPoolExecutor
     wanted: Dict[Tuple[str, str], Tuple[int, ...]] = {}
     subs = [sub for sub, _ in subfields]
+    kind_of = dict(subfields)
     for rank, metas in layout.layout.items():
         if ranks is not None and rank not in ranks:
             continue
@@ -110,7 +111,10 @@ def host_states(layout, subfields=SUBFIELDS, seed: int = 0, distinct_steps: bool
         name, sub = key
         if sub == "param" and (name, "master") in wanted:
             return None  # rounded from the master draw below
-        return host_full(name, sub, wanted[key], seed, distinct_steps)
+        v = host_full(name, sub, wanted[key], seed, distinct_steps)
+        if kind_of[sub] == "bf16" and sub != "param":
+            v = bf16_bits(v)  # bf16 optimizer state (the reference's worker keeps m and v in bf16)
+        return v
 
     keys = list(wanted)
     n = threads or (os.cpu_count() or 1)

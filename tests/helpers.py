@@ -55,8 +55,10 @@ def copy_rect(dst: np.ndarray, do: int, dpitch: int, src: np.ndarray, so: int, s
     d[...] = s
 
 
-def emulate_program(prog, names, states, rank) -> Dict[str, Dict[str, np.ndarray]]:
-    """Apply a Program's slots and segments with numpy; returns {name: {sub: array}}."""
+def emulate_program(prog, names, states, rank, subs=None) -> Dict[str, Dict[str, np.ndarray]]:
+    """Apply a Program's slots and segments with numpy; returns {name: {sub: array}}. subs: the
+    (name, kind) sub-field list the program was built for (default: the benchmark's)."""
+    SUBS = subs or globals()["SUBS"]
     src_buf = []
     for ss in prog.src_slots:
         name = names[ss["name_id"]]

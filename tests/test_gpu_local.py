@@ -154,3 +154,28 @@ def test_reshard_local_extension_layouts_match_reslice(case):
                 if sub == "step":
                     continue
                 assert np.array_equal(host(out[rank][name][sub]).reshape(-1).view(np.uint8), a.reshape(-1).view(np.uint8)), (rank, name, sub)
+
+
+WORKER_SUBS = [("param", "bf16"), ("step", "meta"), ("exp_avg", "bf16"), ("exp_avg_sq", "bf16")]
+
+
+@pytest.mark.parametrize("case", ["cfg3_mini", "cfg5_mini"])
+def test_reshard_local_on_the_reference_worker_state(case):
+    """The state the reference's worker migrates (bf16 param and Adam moments, no master): the
+    kernel's targets equal the oracle's."""
+    cfg = CASES[case]["config"]
+    spl, tpl = cfg.layouts()
+    states = S.host_states(spl, WORKER_SUBS, seed=2, distinct_steps=True)
+    kinds = dict(WORKER_SUBS)
+    dev_states = {r: {n: {s: S.to_torch(a, kinds[s], DEV if kinds[s] != "meta" else None) for s, a in e.items()}
+                      for n, e in st.items()} for r, st in states.items()}
+    out = M.reshard_local(spl, tpl, dev_states, S.expected_sub_fields(WORKER_SUBS), DEV, minimum_est_peers=1)
+    torch.cuda.synchronize()
+    ops = O.schedule(spl, tpl, minimum_est_peers=1)
+    for rank, metas in tpl.layout.items():
+        if not metas:
+            continue
+        want = O.execute_rank(ops, states, [(s, k == "meta") for s, k in WORKER_SUBS], rank)
+        for name, ent in want.items():
+            for sub, a in ent.items():
+                assert np.array_equal(host(out[rank][name][sub]).reshape(-1).view(np.uint8), a.reshape(-1).view(np.uint8)), (rank, name, sub)

@@ -168,3 +168,31 @@ def test_resolve_marks_remote_pieces():
         want = (prog.src_slots["src_rank"][prog.segments["src_slot"]] != rank).astype(np.uint64)
         assert np.array_equal(out["flags"], want)
         assert want.any()
+
+
+# The state the reference's own worker migrates: bf16 param, step, bf16 exp_avg / exp_avg_sq
+# (no fp32 master; tasks/task.py keeps bf16 as the default dtype and uses torch.optim.AdamW).
+WORKER_SUBS = [("param", "bf16"), ("step", "meta"), ("exp_avg", "bf16"), ("exp_avg_sq", "bf16")]
+
+
+@pytest.mark.parametrize("case", ["cfg3_mini", "cfg5_mini", "shrink_mini", "hetero_mini"])
+def test_program_on_the_reference_worker_state(case):
+    """Every sub-field moves as bytes of its own size: the worker's 6-byte state through the same
+    programs, against the oracle (pinned on the benchmark's sub-fields)."""
+    from suika_b200 import synthetic as S
+    cfg = CASES[case]["config"]
+    spl, tpl = cfg.layouts()
+    states = S.host_states(spl, WORKER_SUBS, seed=2, distinct_steps=True)
+    plan = M.Plan(spl, tpl, minimum_est_peers=1)
+    spec = [(2, False), (4, True), (2, False), (2, False)]
+    ops = O.schedule(spl, tpl, minimum_est_peers=1)
+    for rank, metas in tpl.layout.items():
+        if not metas:
+            continue
+        got = emulate_program(plan.program(rank, spec), plan.names, states, rank, WORKER_SUBS)
+        want = O.execute_rank(ops, states, [(s, k == "meta") for s, k in WORKER_SUBS], rank)
+        assert list(got) == list(want)
+        for name, ent in want.items():
+            for sub, a in ent.items():
+                g = got[name][sub]
+                assert g.shape == a.shape and np.array_equal(g.reshape(-1).view(np.uint8), a.reshape(-1).view(np.uint8)), (rank, name, sub)
