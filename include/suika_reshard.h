@@ -105,7 +105,7 @@ typedef struct rs_plan rs_plan;
 typedef struct rs_program rs_program;
 
 const char* rs_last_error(void);
-/* 1.1: rs_copy_launch_noalloc, rs_act_plan, rs_act_resolve added to 1.0; nothing changed. */
+/* 1.1 adds rs_copy_launch_noalloc, rs_act_plan and rs_act_resolve; the 1.0 entry points are unchanged. */
 int rs_version(int32_t* major, int32_t* minor);
 
 /* ---- planning: schedule_param_transfer (migration.py:322-381) -------------------------- */
