@@ -46,3 +46,36 @@ def test_copy_workspace_size_without_gpu():
     n = ctypes.c_uint64()
     assert lib.rs_copy_workspace_bytes(1000, ctypes.byref(n)) == 0
     assert n.value >= 1000 * 72 and n.value % 256 == 0
+
+
+def _descs(rows):
+    import numpy as np
+    return np.array(rows, dtype=_lib.COPY_DESC_DTYPE)
+
+
+def test_copy_staging_validates_before_any_cuda_call():
+    """Malformed copy descriptors are rejected on the host, before the device is touched (so
+    these checks run without a GPU); an all-empty table is a no-op."""
+    lib = _lib.load()
+    info = _lib.RsLaunchInfo()
+    ws = ctypes.c_void_p(1 << 20)  # never dereferenced: validation fails first
+    bad_pitch = _descs([(1 << 20, 2 << 20, 4, 512, 256, 512, 0)])  # 512-byte rows at a 256-byte source pitch
+    assert lib.rs_copy_stage(bad_pitch.ctypes.data, 1, ws, 1 << 20, None, ctypes.byref(info)) == _lib.RS_ERR_ARG
+    assert b"longer than their pitch" in lib.rs_last_error()
+    null_src = _descs([(0, 2 << 20, 1, 64, 64, 64, 0)])
+    assert lib.rs_copy_stage(null_src.ctypes.data, 1, ws, 1 << 20, None, ctypes.byref(info)) == _lib.RS_ERR_ARG
+    assert b"NULL address" in lib.rs_last_error()
+    huge_rows = _descs([(1 << 20, 2 << 20, 1 << 33, 1, 1, 1, 0)])
+    assert lib.rs_copy_stage(huge_rows.ctypes.data, 1, ws, 1 << 20, None, ctypes.byref(info)) == _lib.RS_ERR_ARG
+    empty = _descs([(1 << 20, 2 << 20, 0, 64, 64, 64, 0), (1 << 20, 2 << 20, 3, 0, 64, 64, 0)])
+    assert lib.rs_copy_stage(empty.ctypes.data, 2, None, 0, None, ctypes.byref(info)) == _lib.RS_OK
+    assert info.n_entries == 0 and info.n_tiles == 0
+    assert lib.rs_copy_run(None, ctypes.byref(info), None) == _lib.RS_OK  # nothing staged: nothing to launch
+
+
+def test_noalloc_capacity_and_empty_tables_without_gpu():
+    lib = _lib.load()
+    over = _descs([(1 << 20, 2 << 20, 1, 16, 16, 16, 0)] * (_lib.RS_NOALLOC_MAX_ENTRIES + 1))
+    assert lib.rs_copy_launch_noalloc(over.ctypes.data, len(over), None, None) == _lib.RS_ERR_CAPACITY
+    empty = _descs([(1 << 20, 2 << 20, 0, 16, 16, 16, 0)] * 4)
+    assert lib.rs_copy_launch_noalloc(empty.ctypes.data, len(empty), None, None) == _lib.RS_OK
