@@ -33,4 +33,13 @@ CASES = {
                     "description": "Llama (reduced) DP groups of unequal TP (TP1 + TP2) -> TP4"},
     "odd_mini": {"config": _cfg("odd_mini", _odd, src=[[[0]], [[1]]], dst=[[[0, 1]]]),
                  "description": "odd widths (rows not 16-byte multiples) TP1xPP2 -> TP2"},
+    "pp_deepen_mini": {"config": _cfg("pp_deepen_mini", _llama_mini, src=[[[0, 1]], [[2, 3]]],
+                                      dst=[[[0, 1]], [[2, 3]], [[4, 5]], [[6, 7]]]),
+                       "description": "Llama (reduced) TP2xPP2 on 4 -> TP2xPP4 on 8 (stage boundaries move)"},
+    "gpt_shrink_mini": {"config": _cfg("gpt_shrink_mini", _gpt_mini, src=[[[0, 1, 2, 3]]], dst=[[[0, 1]]]),
+                        "description": "GPT (reduced, wpe, fused c_attn, row biases) TP4 -> TP2 (shrink)"},
+    "grow_dp_tp_mini": {"config": _cfg("grow_dp_tp_mini", _llama_mini, src=[[[0]]], dst=[[[0, 1], [2, 3]]]),
+                        "description": "Llama (reduced) TP1 on 1 -> TP2xDP2 on 4 (TP and DP grow from one rank)"},
+    "qwen_grow_mini": {"config": _cfg("qwen_grow_mini", _qwen_mini, src=[[[0, 1]]], dst=[[[0, 1, 2, 3]]]),
+                       "description": "Qwen2 (reduced, GQA 8/4 heads, QKV bias) TP2 -> TP4 (grow)"},
 }

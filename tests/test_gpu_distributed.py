@@ -72,7 +72,8 @@ def run_case(case, port, direction="pull"):
 
 @pytest.mark.parametrize("direction", ["pull", "push"])
 @pytest.mark.parametrize("case", ["cfg2b_mini", "odd_mini", "cfg1", "cfg2_mini", "cfg3_mini", "cfg4_mini", "cfg5_mini",
-                                  "shrink_mini", "hetero_mini", "cfg2_mini_noib"])
+                                  "shrink_mini", "hetero_mini", "cfg2_mini_noib", "pp_deepen_mini", "gpt_shrink_mini",
+                                  "grow_dp_tp_mini", "qwen_grow_mini"])
 def test_drop_in_matches_reference(case, direction):
     g = load_golden(case)
     results = run_case(case, 29800 + 2 * sorted(CASES).index(case) + (direction == "push"), direction)

@@ -76,12 +76,13 @@ def _check(case, fanout):
     return fo
 
 
-@pytest.mark.parametrize("case", ["odd_mini", "cfg2b_mini", "cfg3_mini", "cfg4_mini", "shrink_mini", "hetero_mini"])
+@pytest.mark.parametrize("case", ["odd_mini", "cfg2b_mini", "cfg3_mini", "cfg4_mini", "shrink_mini", "hetero_mini",
+                                  "pp_deepen_mini", "gpt_shrink_mini", "grow_dp_tp_mini", "qwen_grow_mini"])
 def test_push_tables_rebuild_reference_targets(case):
     _check(case, fanout=False)
 
 
-@pytest.mark.parametrize("case", ["cfg2_mini", "cfg4_mini", "cfg5_mini", "hetero_mini", "shrink_mini"])
+@pytest.mark.parametrize("case", ["cfg2_mini", "cfg4_mini", "cfg5_mini", "hetero_mini", "shrink_mini", "grow_dp_tp_mini"])
 def test_fanout_tables_rebuild_reference_targets(case):
     """Forced fan-out (every exact replica forwarded): still the reference's bytes everywhere."""
     fo = _check(case, fanout=True)
