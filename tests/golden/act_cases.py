@@ -41,6 +41,15 @@ ACT_CASES = {
     # 4-d activation, batch dim 0, slice dim 2 (inner dims after the slice dim)
     "four_dims": dict(mesh_src=[[0, 1]], bszs_src=[2], mesh_dst=[[2, 3, 4, 5]], bszs_dst=[2],
                       shape=[-1, 3, 8, 2], batch_dim=0, slice_dim=2, dtype="float32"),
+    # heterogeneous TP inside the receiving stage
+    "hetero_dst": dict(mesh_src=[[0, 1, 2, 3]], bszs_src=[4], mesh_dst=[[4, 5], [6]], bszs_dst=[2, 2],
+                       shape=[-1, 3, 16], batch_dim=0, slice_dim=-1, dtype="float32"),
+    # one sender to a TP8 group (every receiver takes its chunk, then the all-gather)
+    "tp1_to_tp8": dict(mesh_src=[[0]], bszs_src=[2], mesh_dst=[[1, 2, 3, 4, 5, 6, 7, 8]], bszs_dst=[2],
+                       shape=[-1, 2, 64], batch_dim=0, slice_dim=-1, dtype="bfloat16"),
+    # sequence-first with TP on both sides and DP on the sending side
+    "seq_first_tp_both": dict(mesh_src=[[0, 1], [2, 3]], bszs_src=[2, 2], mesh_dst=[[4, 5, 6, 7]], bszs_dst=[4],
+                              shape=[3, -1, 16], batch_dim=1, slice_dim=2, dtype="float32"),
 }
 
 
