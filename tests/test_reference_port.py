@@ -48,14 +48,17 @@ def _worker(rank, world, case, port, outdir):
         json.dump(res, f)
 
 
-@pytest.mark.parametrize("case", ["odd_mini", "hetero_mini"])
+PORT_CASES = ["odd_mini", "hetero_mini", "grow_dp_tp_mini"]
+
+
+@pytest.mark.parametrize("case", PORT_CASES)
 def test_nccl_port_matches_reference_digests(case):
     import torch.multiprocessing as mp
     spl, tpl = CASES[case]["config"].layouts()
     world = max(len(spl.layout), len(tpl.layout))
     g = load_golden(case)
     with tempfile.TemporaryDirectory() as d:
-        mp.spawn(_worker, args=(world, case, 29730 + 7 * ["odd_mini", "hetero_mini"].index(case), d), nprocs=world, join=True)
+        mp.spawn(_worker, args=(world, case, 29730 + 7 * PORT_CASES.index(case), d), nprocs=world, join=True)
         results = {r: json.load(open(os.path.join(d, f"rank{r}.json"))) for r in range(world)}
     for r, res in results.items():
         assert "error" not in res, res.get("error")
