@@ -144,3 +144,50 @@ def test_mesh_from_reference_object():
         def to_list(self):
             return [[0, 1], [2, 3]]
     assert A.mesh_lists(Raw()) == [[0, 1], [2, 3]]
+
+
+def _random_stage(rng, first_rank):
+    groups, r = [], first_rank
+    for _ in range(int(rng.integers(1, 4))):
+        tp = int(rng.choice([1, 2, 4]))
+        groups.append(list(range(r, r + tp)))
+        r += tp
+    bszs = [int(rng.integers(0, 4)) for _ in groups]
+    return groups, bszs, r
+
+
+def random_act_cases(n=40, seed=77):
+    rng = np.random.default_rng(seed)
+    out = []
+    while len(out) < n:
+        ms, bs, nxt = _random_stage(rng, 0)
+        md, bd, _ = _random_stage(rng, nxt)
+        nd = int(rng.integers(2, 5))
+        batch_dim, slice_dim = (int(x) for x in rng.choice(nd, size=2, replace=False))
+        shape = [int(rng.integers(1, 4)) for _ in range(nd)]
+        shape[slice_dim] = 4 * int(rng.integers(1, 4))  # divisible by every TP degree used
+        shape[batch_dim] = -1
+        out.append(dict(mesh_src=ms, bszs_src=bs, mesh_dst=md, bszs_dst=bd, shape=shape, batch_dim=batch_dim,
+                        slice_dim=slice_dim, dtype="float32"))
+    return out
+
+
+@pytest.mark.parametrize("k", range(40))
+def test_random_exchanges_match_the_oracle(k):
+    """Seeded random stage pairs (DP groups of unequal TP, empty and uneven batches, 2-4 dims, any
+    batch / slice dim): the one-device table equals the oracle's exchange."""
+    case = random_act_cases()[k]
+    src, dst = _stages(case)
+    srcs, tgts = source_arrays(case, seed=k), zero_targets(case)
+    want = zero_targets(case)
+    OA.exchange_world(srcs, want, case["mesh_src"], case["mesh_dst"], case["bszs_src"], case["bszs_dst"],
+                      case["batch_dim"], case["slice_dim"])
+    mem = Memory()
+    sa = {r: mem.add(a.reshape(-1).view(np.uint8)) for r, a in srcs.items()}
+    da = {r: mem.add(a.reshape(-1).view(np.uint8)) for r, a in tgts.items()}
+    pieces = A._plan(src, dst, _slice_size(case))
+    assert [tuple(int(x) for x in p) for p in pieces] == OA.provenance(case["mesh_src"], case["mesh_dst"], case["bszs_src"],
+                                                                         case["bszs_dst"], _slice_size(case))
+    _apply(mem, A._resolve(src, dst, _geo(case, 4), pieces, sa, da))
+    for r in tgts:
+        assert np.array_equal(tgts[r], want[r]), r
