@@ -91,3 +91,13 @@ def test_rules_need_interval_mode():
     spl, tpl = EXT_CASES["gqa_pp"].layouts()
     with pytest.raises(ValueError, match="interval"):
         M.Plan(spl, tpl, mode="reference")
+
+
+@pytest.mark.parametrize("k", range(24))
+def test_random_extension_reshards_equal_reslice(k):
+    """Seeded random (TP, PP, DP) reshards of the GQA + fused-QKV + vocab-parallel model: the
+    interval planner's programs equal re-slicing the full tensors. TP 4 replicates the 2 KV
+    heads on one side or both."""
+    from tests.test_planner_random import cases
+    src, dst, _ = cases(n=24, seed=4321)[k]
+    _check(ReshardConfig(f"rand_ext_{k}", _gqa, src, dst))
