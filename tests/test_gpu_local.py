@@ -179,3 +179,25 @@ def test_reshard_local_on_the_reference_worker_state(case):
         for name, ent in want.items():
             for sub, a in ent.items():
                 assert np.array_equal(host(out[rank][name][sub]).reshape(-1).view(np.uint8), a.reshape(-1).view(np.uint8)), (rank, name, sub)
+
+
+@pytest.mark.parametrize("k", range(8))
+def test_random_reshards_on_the_kernel(k):
+    """Seeded random (TP, PP, DP) reshards through the kernel, every rank on one GPU: targets equal
+    the oracle's in the reference's cat order."""
+    from tests.test_planner_random import SPEC as RSPEC, cases
+    from suika_b200.layouts import ReshardConfig
+    src, dst, peers = cases(n=8, seed=99)[k]
+    spl, tpl = ReshardConfig("rand", RSPEC, src, dst).layouts()
+    states = S.host_states(spl, SUBS, seed=k, distinct_steps=True, threads=1)
+    out = M.reshard_local(spl, tpl, to_device(states), S.expected_sub_fields(), DEV, minimum_est_peers=peers)
+    torch.cuda.synchronize()
+    ops = O.schedule(spl, tpl, minimum_est_peers=peers)
+    for rank, metas in tpl.layout.items():
+        if not metas:
+            continue
+        want = O.execute_rank(ops, states, SUB_META, rank)
+        assert list(out[rank]) == list(want)
+        for name, ent in want.items():
+            for sub, a in ent.items():
+                assert np.array_equal(host(out[rank][name][sub]).reshape(-1).view(np.uint8), a.reshape(-1).view(np.uint8)), (rank, name, sub)
