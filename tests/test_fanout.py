@@ -110,3 +110,45 @@ def test_fanout_switch_values():
     assert M._fanout_setting(" AUTO ") == "auto" and M._fanout_setting("1") is True
     with pytest.raises(ValueError, match="SUIKA_RESHARD_FANOUT"):
         M._fanout_setting("yes")
+
+
+def test_fanout_on_an_interval_plan_equals_reslice():
+    """GQA with fused QKV and vocab-parallel wte (interval planner), TP4 -> TP2 x DP2 with forced
+    fan-out: every target equals the re-sliced full tensor."""
+    from tests.test_extension_layouts import EXT_CASES
+    cfg = EXT_CASES["gqa_rep_src"]
+    spl, tpl = cfg.layouts()
+    plan = M.Plan(spl, tpl)
+    assert plan.mode == "interval"
+    fo = plan_fanout(plan, STATE_BYTES, True)
+    assert fo.active
+    states = S.host_states(spl, SUBS, seed=3, distinct_steps=True)
+    mem = Memory()
+    src_addr = {}
+    for r, st in states.items():
+        for name, ent in st.items():
+            for sub, a in ent.items():
+                b = np.ascontiguousarray(a).reshape(-1).view(np.uint8).copy()
+                src_addr[(r, name, sub)] = (mem.add(b), b.nbytes)
+    arenas, progs = {}, {}
+    for T in tpl.layout:
+        progs[T] = plan.program(T, SPEC)
+        off, nb, total = M._arena_layout(progs[T].dst_slots)
+        arenas[T] = (mem.add(np.full(max(total, 1), 0xAB, dtype=np.uint8)), off, nb)
+    stage2 = []
+    for rank in sorted(arenas):
+        t1, _peer, s2 = M._push_rank_tables(plan, rank, SPEC, SUBNAMES, lambda n, s, r=rank: src_addr[(r, n, s)],
+                                            lambda T: arenas[T][0], lambda T: arenas[T][1], lambda T: arenas[T][2],
+                                            progs[rank], fo)
+        _apply(mem, t1)
+        stage2 += [(fo.phase2[(rank, F, rnd)], d) for (F, rnd), d in s2.items()]
+    for k in range(fo.n2):
+        for p, d in stage2:
+            if p == k:
+                _apply(mem, d)
+    for T in tpl.layout:
+        want = O.semantic_target(states, spl, tpl, SUB_META, T)
+        base, off, nb = arenas[T]
+        for ds, o, n in zip(progs[T].dst_slots, off, nb):
+            name, sub = plan.names[ds["name_id"]], SUBNAMES[ds["subfield"]]
+            assert np.array_equal(mem.view(base + int(o), int(n)), want[name][sub].reshape(-1).view(np.uint8)), (T, name, sub)
