@@ -22,6 +22,35 @@ def _plan(src, dst, spec=SPECS["llama2-7b"], order="reference"):
     return spl, tpl, M.Plan(spl, tpl, order=order, minimum_est_peers=1)
 
 
+def _emulate_push(plan, tpl, states, fo):
+    """Both stages of a push transfer on emulated memory: every rank's stage-1 table, then the
+    stage-2 phases in order. Returns (memory, arenas, programs)."""
+    mem = Memory()
+    src_addr = {}
+    for r, st in states.items():
+        for name, ent in st.items():
+            for sub, a in ent.items():
+                b = np.ascontiguousarray(a).reshape(-1).view(np.uint8).copy()
+                src_addr[(r, name, sub)] = (mem.add(b), b.nbytes)
+    arenas, progs = {}, {}
+    for T in tpl.layout:
+        progs[T] = plan.program(T, SPEC)
+        off, nb, total = M._arena_layout(progs[T].dst_slots)
+        arenas[T] = (mem.add(np.full(max(total, 1), 0xAB, dtype=np.uint8)), off, nb)
+    stage2 = []
+    for rank in sorted(arenas):
+        t1, _peer, s2 = M._push_rank_tables(plan, rank, SPEC, SUBNAMES, lambda n, s, r=rank: src_addr[(r, n, s)],
+                                            lambda T: arenas[T][0], lambda T: arenas[T][1], lambda T: arenas[T][2],
+                                            progs[rank], fo)
+        _apply(mem, t1)
+        stage2 += [(fo.phase2[(rank, F, rnd)], d) for (F, rnd), d in s2.items()]
+    for k in range(fo.n2):
+        for p, d in stage2:
+            if p == k:
+                _apply(mem, d)
+    return mem, arenas, progs
+
+
 def test_auto_keeps_direct_transfers_on_the_baseline_reshards():
     """On cfg2-cfg5 no source sends more than the busiest target receives: fan-out cannot help."""
     for c in ("cfg2", "cfg3", "cfg4", "cfg5"):
@@ -70,29 +99,7 @@ def test_dp_grow_tables_with_fanout_match_the_oracle(order):
     fo = plan_fanout(plan, STATE_BYTES, True)
     assert fo.active
     states = S.host_states(spl, SUBS, seed=11, distinct_steps=True)
-    mem = Memory()
-    src_addr = {}
-    for r, st in states.items():
-        for name, ent in st.items():
-            for sub, a in ent.items():
-                b = np.ascontiguousarray(a).reshape(-1).view(np.uint8).copy()
-                src_addr[(r, name, sub)] = (mem.add(b), b.nbytes)
-    arenas, progs = {}, {}
-    for T in tpl.layout:
-        progs[T] = plan.program(T, SPEC)
-        off, nb, total = M._arena_layout(progs[T].dst_slots)
-        arenas[T] = (mem.add(np.full(max(total, 1), 0xAB, dtype=np.uint8)), off, nb)
-    stage2 = []
-    for rank in sorted(arenas):
-        t1, _peer, s2 = M._push_rank_tables(plan, rank, SPEC, SUBNAMES, lambda n, s, r=rank: src_addr[(r, n, s)],
-                                            lambda T: arenas[T][0], lambda T: arenas[T][1], lambda T: arenas[T][2],
-                                            progs[rank], fo)
-        _apply(mem, t1)
-        stage2 += [(fo.phase2[(rank, F, rnd)], d) for (F, rnd), d in s2.items()]
-    for k in range(fo.n2):
-        for p, d in stage2:
-            if p == k:
-                _apply(mem, d)
+    mem, arenas, progs = _emulate_push(plan, tpl, states, fo)
     ops = O.schedule(spl, tpl, minimum_est_peers=1)
     for T in tpl.layout:
         want = O.execute_rank(ops, states, SUB_META, T, order=order)
@@ -123,29 +130,7 @@ def test_fanout_on_an_interval_plan_equals_reslice():
     fo = plan_fanout(plan, STATE_BYTES, True)
     assert fo.active
     states = S.host_states(spl, SUBS, seed=3, distinct_steps=True)
-    mem = Memory()
-    src_addr = {}
-    for r, st in states.items():
-        for name, ent in st.items():
-            for sub, a in ent.items():
-                b = np.ascontiguousarray(a).reshape(-1).view(np.uint8).copy()
-                src_addr[(r, name, sub)] = (mem.add(b), b.nbytes)
-    arenas, progs = {}, {}
-    for T in tpl.layout:
-        progs[T] = plan.program(T, SPEC)
-        off, nb, total = M._arena_layout(progs[T].dst_slots)
-        arenas[T] = (mem.add(np.full(max(total, 1), 0xAB, dtype=np.uint8)), off, nb)
-    stage2 = []
-    for rank in sorted(arenas):
-        t1, _peer, s2 = M._push_rank_tables(plan, rank, SPEC, SUBNAMES, lambda n, s, r=rank: src_addr[(r, n, s)],
-                                            lambda T: arenas[T][0], lambda T: arenas[T][1], lambda T: arenas[T][2],
-                                            progs[rank], fo)
-        _apply(mem, t1)
-        stage2 += [(fo.phase2[(rank, F, rnd)], d) for (F, rnd), d in s2.items()]
-    for k in range(fo.n2):
-        for p, d in stage2:
-            if p == k:
-                _apply(mem, d)
+    mem, arenas, progs = _emulate_push(plan, tpl, states, fo)
     for T in tpl.layout:
         want = O.semantic_target(states, spl, tpl, SUB_META, T)
         base, off, nb = arenas[T]
