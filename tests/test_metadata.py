@@ -77,6 +77,14 @@ def _worker(rank, world, port, cfg_name, q):
         b = MD.broadcast_param_layout(spl if rank == 0 else None, src=0)
         _same_layout(spl, b)
         assert MD.broadcast_param_layout(None, src=0) is None
+        # a subgroup: its ranks are numbered within the group (as ParamLayout.gather numbers them)
+        sub = dist.new_group([1, 3])
+        if rank in (1, 3):
+            part = MD.gather_param_layout(spl.layout[rank], world=sub)
+            assert part.ranks == [0, 1]
+            assert list(part.layout[0]) == list(spl.layout[1]) and list(part.layout[1]) == list(spl.layout[3])
+            got = MD.broadcast_param_layout(part if rank == 3 else None, src=1, group=sub)  # group rank 1 = rank 3
+            assert got.ranks == [0, 1] and list(got.layout[1]) == list(spl.layout[3])
         dist.barrier()
         dist.destroy_process_group()
         q.put((rank, "ok"))
