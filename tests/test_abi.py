@@ -79,3 +79,18 @@ def test_noalloc_capacity_and_empty_tables_without_gpu():
     assert lib.rs_copy_launch_noalloc(over.ctypes.data, len(over), None, None) == _lib.RS_ERR_CAPACITY
     empty = _descs([(1 << 20, 2 << 20, 0, 16, 16, 16, 0)] * 4)
     assert lib.rs_copy_launch_noalloc(empty.ctypes.data, len(empty), None, None) == _lib.RS_OK
+
+
+def test_header_is_plain_c():
+    """FFI users (ctypes, cgo, JNI) bind the header as C: it must compile as C99 on its own,
+    without warnings, and as C++."""
+    import shutil
+    import subprocess
+    import pytest
+    hdr = os.path.join(REPO, "include", "suika_reshard.h")
+    if not shutil.which("gcc"):
+        pytest.skip("gcc not found")
+    for cmd in (["gcc", "-std=c99", "-Wall", "-Wextra", "-pedantic", "-Werror", "-fsyntax-only", "-x", "c", hdr],
+                ["g++", "-std=c++11", "-Wall", "-Werror", "-fsyntax-only", "-x", "c++", hdr]):
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        assert r.returncode == 0, r.stderr
