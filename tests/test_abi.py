@@ -94,3 +94,41 @@ def test_header_is_plain_c():
                 ["g++", "-std=c++11", "-Wall", "-Werror", "-fsyntax-only", "-x", "c++", hdr]):
         r = subprocess.run(cmd, capture_output=True, text=True)
         assert r.returncode == 0, r.stderr
+
+
+def test_ctypes_structs_match_the_header_layout(tmp_path):
+    """Every ctypes structure in the binding has the size and field offsets the C compiler gives
+    the header's struct of the same name (a header / binding drift would corrupt calls)."""
+    import shutil
+    import subprocess
+    import pytest
+    if not shutil.which("gcc"):
+        pytest.skip("gcc not found")
+    pairs = {
+        "rs_tensor_meta": _lib.RsTensorMeta, "rs_rank_layout": _lib.RsRankLayout, "rs_plan_opts": _lib.RsPlanOpts,
+        "rs_op": _lib.RsOp, "rs_slice_group": _lib.RsSliceGroup, "rs_slice_rule": _lib.RsSliceRule,
+        "rs_subfield": _lib.RsSubfield, "rs_program_counts": _lib.RsProgramCounts, "rs_dst_slot": _lib.RsDstSlot,
+        "rs_src_slot": _lib.RsSrcSlot, "rs_meta_slot": _lib.RsMetaSlot, "rs_segment": _lib.RsSegment,
+        "rs_copy_desc": _lib.RsCopyDesc, "rs_launch_info": _lib.RsLaunchInfo, "rs_peer_handle": _lib.RsPeerHandle,
+        "rs_stage_mesh": _lib.RsStageMesh, "rs_act_piece": _lib.RsActPiece, "rs_act_geometry": _lib.RsActGeometry,
+    }
+    lines = ['#include <stdio.h>', '#include <stddef.h>', f'#include "{os.path.join(REPO, "include", "suika_reshard.h")}"',
+             "int main(void) {"]
+    for cname, cls in pairs.items():
+        lines.append(f'  printf("{cname} (sizeof) %zu\\n", sizeof({cname}));')
+        for f, _t in cls._fields_:
+            lines.append(f'  printf("{cname} {f} %zu\\n", offsetof({cname}, {f}));')
+    lines += ["  return 0;", "}"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    r = subprocess.run(["gcc", "-std=c99", str(src), "-o", str(exe)], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    got = {}
+    for line in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.splitlines():
+        name, field, value = line.split()
+        got[(name, field)] = int(value)
+    for cname, cls in pairs.items():
+        assert got[(cname, "(sizeof)")] == ctypes.sizeof(cls), cname
+        for f, _t in cls._fields_:
+            assert got[(cname, f)] == getattr(cls, f).offset, (cname, f)
