@@ -132,3 +132,13 @@ def test_ctypes_structs_match_the_header_layout(tmp_path):
         assert got[(cname, "(sizeof)")] == ctypes.sizeof(cls), cname
         for f, _t in cls._fields_:
             assert got[(cname, f)] == getattr(cls, f).offset, (cname, f)
+
+
+def test_numpy_mirrors_match_the_ctypes_structures():
+    """The numpy dtypes used to fill large tables have the ctypes structures' field offsets."""
+    for dt, cls in ((_lib.TENSOR_META_DTYPE, _lib.RsTensorMeta), (_lib.COPY_DESC_DTYPE, _lib.RsCopyDesc),
+                    (_lib.SEGMENT_DTYPE, _lib.RsSegment), (_lib.ACT_PIECE_DTYPE, _lib.RsActPiece)):
+        assert dt.itemsize == ctypes.sizeof(cls)
+        assert list(dt.names) == [f for f, _ in cls._fields_]
+        for f, _ in cls._fields_:
+            assert dt.fields[f][1] == getattr(cls, f).offset, (cls.__name__, f)
