@@ -136,8 +136,11 @@ def test_ctypes_structs_match_the_header_layout(tmp_path):
 
 def test_numpy_mirrors_match_the_ctypes_structures():
     """The numpy dtypes used to fill large tables have the ctypes structures' field offsets."""
+    from suika_b200 import migration as M
     for dt, cls in ((_lib.TENSOR_META_DTYPE, _lib.RsTensorMeta), (_lib.COPY_DESC_DTYPE, _lib.RsCopyDesc),
-                    (_lib.SEGMENT_DTYPE, _lib.RsSegment), (_lib.ACT_PIECE_DTYPE, _lib.RsActPiece)):
+                    (_lib.SEGMENT_DTYPE, _lib.RsSegment), (_lib.ACT_PIECE_DTYPE, _lib.RsActPiece),
+                    (M.DST_SLOT_DTYPE, _lib.RsDstSlot), (M.SRC_SLOT_DTYPE, _lib.RsSrcSlot),
+                    (M.META_SLOT_DTYPE, _lib.RsMetaSlot), (M.OP_DTYPE, _lib.RsOp)):
         assert dt.itemsize == ctypes.sizeof(cls)
         assert list(dt.names) == [f for f, _ in cls._fields_]
         for f, _ in cls._fields_:
