@@ -145,3 +145,23 @@ def test_numpy_mirrors_match_the_ctypes_structures():
         assert list(dt.names) == [f for f, _ in cls._fields_]
         for f, _ in cls._fields_:
             assert dt.fields[f][1] == getattr(cls, f).offset, (cls.__name__, f)
+
+
+def test_binding_arities_match_the_header():
+    """Each ctypes signature takes as many arguments as the header's prototype, and returns int
+    unless the prototype returns void or a string."""
+    src = open(os.path.join(REPO, "include", "suika_reshard.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    protos = {}
+    for m in re.finditer(r"^([A-Za-z_][\w\s\*]*?)\b(rs_\w+)\s*\(([^;{]*?)\)\s*;", src, flags=re.M | re.S):
+        ret, name, params = m.group(1).strip(), m.group(2), " ".join(m.group(3).split())
+        n = 0 if params in ("", "void") else params.count(",") + 1
+        protos[name] = (ret, n)
+    assert set(protos) == declared_functions(), "every declared function parsed"
+    for name, (ret, n) in protos.items():
+        res, args = _lib.SIGNATURES[name]
+        assert len(args) == n, (name, len(args), n)
+        if ret == "int":
+            assert res is ctypes.c_int, name
+        elif ret == "void":
+            assert res is None, name
