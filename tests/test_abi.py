@@ -165,3 +165,69 @@ def test_binding_arities_match_the_header():
             assert res is ctypes.c_int, name
         elif ret == "void":
             assert res is None, name
+
+
+C_CLIENT = r"""
+#include <stdio.h>
+#include <string.h>
+#include "suika_reshard.h"
+
+/* A C client of the ABI: plan TP1 -> TP2 of one [8, 4] fp32 weight split on dim 0 and of one
+   replicated [4] norm, then the activation pieces of a TP2 -> TP1 x DP2 stage boundary. */
+int main(void) {
+  rs_tensor_meta src_t[2], dst0[2], dst1[2];
+  memset(src_t, 0, sizeof src_t); memset(dst0, 0, sizeof dst0); memset(dst1, 0, sizeof dst1);
+  for (int i = 0; i < 2; ++i) {
+    rs_tensor_meta* all[3] = {&src_t[i], &dst0[i], &dst1[i]};
+    for (int k = 0; k < 3; ++k) {
+      all[k]->name_id = i; all[k]->itemsize = 4;
+      all[k]->ndim = i == 0 ? 2 : 1; all[k]->shape[0] = i == 0 ? 8 : 4; all[k]->shape[1] = 4;
+      all[k]->slice_dim = RS_NO_SLICE; all[k]->tp_index = 0; all[k]->tp_deg = 1;
+    }
+  }
+  dst0[0].slice_dim = 0; dst0[0].tp_index = 0; dst0[0].tp_deg = 2;
+  dst1[0].slice_dim = 0; dst1[0].tp_index = 1; dst1[0].tp_deg = 2;
+  rs_rank_layout src = {0, 2, src_t};
+  rs_rank_layout dst[2] = {{0, 2, dst0}, {1, 2, dst1}};
+  rs_plan_opts opts = {1, RS_ORDER_REFERENCE, RS_SRC_REFERENCE, 0};
+  rs_plan* plan = NULL;
+  if (rs_plan_build(&src, 1, dst, 2, &opts, &plan) != RS_OK) { printf("plan: %s\n", rs_last_error()); return 1; }
+  int64_t n = 0;
+  rs_plan_num_ops(plan, &n);
+  rs_op ops[8];
+  if (n != 4 || rs_plan_get_ops(plan, ops, 8) != RS_OK) { printf("ops: %lld\n", (long long)n); return 2; }
+  rs_plan_free(plan);
+
+  int32_t gs_src[2] = {0, 2}, ranks_src[2] = {0, 1}; int64_t b_src[1] = {4};
+  int32_t gs_dst[3] = {0, 1, 2}, ranks_dst[2] = {2, 3}; int64_t b_dst[2] = {2, 2};
+  rs_stage_mesh ms = {1, 0, gs_src, ranks_src, b_src}, md = {2, 0, gs_dst, ranks_dst, b_dst};
+  int64_t np_ = 0;
+  if (rs_act_plan(&ms, &md, 16, NULL, 0, &np_) != RS_OK || np_ != 4) { printf("act: %lld\n", (long long)np_); return 3; }
+  if (rs_act_plan(&ms, &md, 15, NULL, 0, &np_) != RS_ERR_SHAPE) return 4;  /* 15 does not split in two */
+  int32_t maj = 0, min = 0;
+  rs_version(&maj, &min);
+  printf("ok %d.%d ops=%lld pieces=4\n", maj, min, (long long)n);
+  return 0;
+}
+"""
+
+
+def test_a_c_program_links_and_plans(tmp_path):
+    """The boundary is C: a C program links libsuika_reshard.so and plans through it (no GPU
+    needed for planning)."""
+    import shutil
+    import subprocess
+    import pytest
+    if not shutil.which("gcc"):
+        pytest.skip("gcc not found")
+    lib = _lib.library_path()
+    _lib.load()  # builds the library when it is stale
+    src = tmp_path / "client.c"
+    src.write_text(C_CLIENT)
+    exe = tmp_path / "client"
+    libdir = os.path.dirname(lib)
+    r = subprocess.run(["gcc", "-std=c99", "-Wall", "-Werror", f"-I{os.path.join(REPO, 'include')}", str(src), "-o", str(exe),
+                        f"-L{libdir}", "-l:" + os.path.basename(lib), f"-Wl,-rpath,{libdir}"], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    run = subprocess.run([str(exe)], capture_output=True, text=True)
+    assert run.returncode == 0 and run.stdout.startswith("ok 1."), (run.returncode, run.stdout, run.stderr)
