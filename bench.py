@@ -40,7 +40,8 @@ from suika_b200.layouts import CONFIGS, EXTRA_CONFIGS, SPECS, ReshardConfig, sca
 
 METRIC = "state-migration time (s) and NVLink GB/s per GPU for 3D-layout reshard"
 FALLBACK_HBM_GBS = 6650.0
-NVLINK_PEER_GBS = 770.0   # measured peer copy per direction per GPU on this pool (900 nominal)
+NVLINK_GBS = 900.0               # NVLink 5 per direction per GPU: the roofline of remote traffic
+NVLINK_MEASURED_PEER_GBS = 770.0  # a peer copy per direction measured on this pool, for context
 L2_BYTES = 126 * 2 ** 20
 
 
@@ -83,6 +84,17 @@ def workload(n_gpus: int, layers: int = 0, config: str = "") -> ReshardConfig:
     dst = [[list(range(half))], [list(range(half, n_gpus))]]
     name = "cfg3" if (n_gpus == 8 and spec.n_layers == 40) else f"llama2-13b-{spec.n_layers}L"
     return ReshardConfig(name, spec, src, dst, f"Llama2-13B-shaped {spec.n_layers} layers TP{n_gpus} -> TP{half}xPP2")
+
+
+def workload_config(cfg: ReshardConfig, n_gpus: int) -> dict:
+    """The `config` object of a result line; both arms print the same one for the same workload."""
+    if n_gpus == 1:
+        what = (f"{cfg.name}: {cfg.spec.name} ({cfg.spec.n_layers} layers) full training state (bf16 param + fp32 "
+                f"master/m/v + step), TP1 -> TP2 on one GPU, dim-0 slices and replicated tensors as views, row-split "
+                f"pieces packed")
+    else:
+        what = f"{cfg.name}: {cfg.note}, full training state (bf16 param + fp32 master/m/v + step)"
+    return {"workload": what, "l2": "inputs larger than L2 (no flush needed)", "order": "reference"}
 
 
 # ---------------------------------------------------------------------------------------------
@@ -140,15 +152,23 @@ class Clocks:
 # ---------------------------------------------------------------------------------------------
 # CPU baseline: the oracle (a restatement of the reference's algorithm) on the host cores
 # ---------------------------------------------------------------------------------------------
+STATE_BYTES_PER_ELEM = 2 + 4 + 4 + 4  # bf16 param + fp32 master, exp_avg, exp_avg_sq
+
+
 def moved_bytes_views(plan: M.Plan, spl, tpl) -> int:
     """Bytes a TP1 -> TP2 'views' relayout must write: every piece that is not one contiguous range
     of its source (row-split pieces); the reference writes all target bytes."""
-    its = [2, 4, 4, 4]
     total = 0
     for o in plan.op_array:
         if o["dst_slice_dim"] == -1 and o["src_tp_deg"] < o["dst_tp_deg"]:
-            total += int(o["numel"]) * sum(its)
+            total += int(o["numel"]) * STATE_BYTES_PER_ELEM
     return total
+
+
+def moved_bytes_views_ops(ops) -> int:
+    """moved_bytes_views over the oracle's op list (the reference arm loads no product code)."""
+    return sum(o.numel * STATE_BYTES_PER_ELEM for o in ops
+               if o.dst_tp is not None and o.dst_tp[0] == -1 and (o.src_tp[2] if o.src_tp else 1) < o.dst_tp[2])
 
 
 def cpu_sample(cfg: ReshardConfig, n_gpus: int):
@@ -174,20 +194,21 @@ class OracleSample:
         self.spl, self.tpl = self.sample.layouts(with_embeddings=(n_gpus == 1))
         self.subs = [(s, k == "meta") for s, k in S.SUBFIELDS]
         self.threads = threads
-        plan = M.Plan(self.spl, self.tpl, minimum_est_peers=1)
-        ops = plan.op_array
+        # units and ranks come from the oracle's own schedule: nothing here loads the product library
+        ops = O.schedule(self.spl, self.tpl, minimum_est_peers=1)
         if n_gpus == 1:
-            self.units = moved_bytes_views(plan, self.spl, self.tpl)
+            self.units = moved_bytes_views_ops(ops)
             self.ranks = [r for r, m in self.tpl.layout.items() if m]
             src_ranks = None
             self.what = self.sample.note
         else:
-            remote = ops["src_rank"] != ops["dst_rank"]
-            ing = {int(r): int(ops["numel"][remote & (ops["dst_rank"] == r)].sum()) for r in np.unique(ops["dst_rank"])}
+            ing = {}
+            for o in ops:
+                ing[o.dst] = ing.get(o.dst, 0) + (o.numel if o.src != o.dst else 0)
             r = max(ing, key=lambda k: (ing[k], -k))
             self.ranks = [r]
-            src_ranks = sorted(set(int(x) for x in ops["src_rank"][ops["dst_rank"] == r]))
-            self.units = int(ops["numel"][ops["dst_rank"] == r].sum()) * 14
+            src_ranks = sorted({o.src for o in ops if o.dst == r})
+            self.units = sum(o.numel for o in ops if o.dst == r) * STATE_BYTES_PER_ELEM
             self.what = f"target rank {r}'s share of 2 layers (1 per target stage, no embeddings) of {cfg.note}"
         self.states = S.host_states(self.spl, S.SUBFIELDS, seed=0, ranks=src_ranks, threads=threads)
 
@@ -213,19 +234,25 @@ def cpu_baseline_block(cfg, n_gpus, threads, budget_s=20.0):
             "sample": smp.describe(reps)}
 
 
-def traffic_per_unit(kernel_key: str):
-    """DRAM bytes (read + write) per moved byte of the kernel, from the committed ncu summary
-    profiles/<kernel_key>.md (a line `dram_bytes_per_moved_byte: X`), or None."""
-    p = os.path.join(REPO, "profiles", f"{kernel_key}.md")
-    if not os.path.exists(p):
-        return None
-    for line in open(p):
-        if line.strip().startswith("dram_bytes_per_moved_byte:"):
-            try:
-                return float(line.split(":", 1)[1].strip().split()[0])
-            except ValueError:
-                return None
-    return None
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per moved byte of the one-GPU pack,
+# from one ncu capture of the same kernel on a 2-layer cfg2b case (1.732 GB moved per launch, above
+# L2): `ncu --set full --clock-control none -k regex:rs_copy -s 3 -c 1 python bench.py --layers 2
+# --steps 3 --warmup 3 --no-e2e --no-cpu-baseline --no-check`. Traffic grows with the moved bytes
+# (every byte is read once and written once), so the full launch's traffic is this ratio x moved.
+DRAM_BYTES_PER_MOVED_BYTE = 1.967
+
+
+def rank_bytes_ops(ops) -> dict:
+    """Per-rank ingress / egress / local bytes of an oracle op list (14 B per element)."""
+    out = {"ingress": {}, "egress": {}, "local": {}}
+    for o in ops:
+        b = o.numel * STATE_BYTES_PER_ELEM
+        if o.src == o.dst:
+            out["local"][o.dst] = out["local"].get(o.dst, 0) + b
+        else:
+            out["ingress"][o.dst] = out["ingress"].get(o.dst, 0) + b
+            out["egress"][o.src] = out["egress"].get(o.src, 0) + b
+    return out
 
 
 # ---------------------------------------------------------------------------------------------
@@ -290,21 +317,19 @@ def run_single(args):
     kern_s = statistics.mean(launch_ms) / 1e3
     peak, peak_src = peaks()
     achieved = 2 * moved / kern_s / 1e9
-    tpu = traffic_per_unit("copy_kernel_cfg2b")
+    tpu = DRAM_BYTES_PER_MOVED_BYTE
     res = {
         "metric": METRIC, "value": round(moved * args.steps / total_s / 1e9, 2), "unit": "GB/s",
         "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(total_s / args.steps * 1e3, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8",
         "data": "synthetic (seeded N(0,0.02) weights, norms 1.0, m~N(0,1e-3), v~|N(0,1e-6)|)",
-        "config": {"workload": "cfg2b: Llama2-7B full training state (bf16 param + fp32 master/m/v + step), TP1 -> TP2 "
-                               "on one GPU, dim-0 slices and replicated tensors as views, row-split pieces packed",
-                   "source_state_gb": round(state.nbytes() / 1e9, 2), "moved_gb_per_step": round(moved / 1e9, 3),
-                   "l2": "inputs larger than L2 (no flush needed)", "order": "reference"},
+        "config": workload_config(cfg, 1),
+        "workload_bytes": {"source_state_gb": round(state.nbytes() / 1e9, 2), "moved_gb_per_step": round(moved / 1e9, 3)},
         "migration_s": round(total_s / args.steps, 6),
         "nvlink_gbs_per_gpu": 0.0,
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs, burst copy)",
-                     "traffic": None if tpu is None else int(tpu * moved),
+                     "traffic": int(tpu * moved),
                      "algorithmic_bytes_per_launch": 2 * moved, "kernel_ms": round(kern_s * 1e3, 4)},
         "gpu_launches": args.steps,
         "clocks": ck.summary(),
@@ -386,7 +411,7 @@ def run_dist(args):
         rt = M.RankTransfer(plan, src, exp, dev, phased=not args.no_phases)
     else:
         from suika_b200.fanout import plan_fanout
-        fo = plan_fanout(plan, sum([2, 4, 4, 4]), mode={"off": False, "auto": "auto", "on": True}[args.fanout])
+        fo = plan_fanout(plan, STATE_BYTES_PER_ELEM, mode={"off": False, "auto": "auto", "on": True}[args.fanout])
         rt = M.RankTransferPush(plan, src, exp, dev, phased=not args.no_phases, fanout=fo if fo.active else None)
     its = [2, 4, 4, 4]
     rb = plan.rank_bytes(its)
@@ -431,17 +456,18 @@ def run_dist(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t * 1e3, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "u8",
             "data": "synthetic (seeded N(0,0.02) weights, norms 1.0, m~N(0,1e-3), v~|N(0,1e-6)|)",
-            "config": {"workload": f"{cfg.name}: {cfg.note}, full training state (bf16 param + fp32 master/m/v + step)",
-                       "cross_gb": round(sum(rb["ingress"].values()) / 1e9, 3), "local_gb": round(sum(rb["local"].values()) / 1e9, 3),
-                       "max_ingress_gb": round(max(rb["ingress"].values(), default=0) / 1e9, 3),
-                       "max_egress_gb": round(max(rb["egress"].values(), default=0) / 1e9, 3),
-                       "l2": "inputs larger than L2 (no flush needed)", "order": "reference", "src_choice": "reference",
-                       "direction": args.direction, "phases": rt.n_phases},
+            "config": workload_config(cfg, world),
+            "workload_bytes": {"cross_gb": round(sum(rb["ingress"].values()) / 1e9, 3),
+                               "local_gb": round(sum(rb["local"].values()) / 1e9, 3),
+                               "max_ingress_gb": round(max(rb["ingress"].values(), default=0) / 1e9, 3),
+                               "max_egress_gb": round(max(rb["egress"].values(), default=0) / 1e9, 3),
+                               "src_choice": "reference", "direction": args.direction, "phases": rt.n_phases},
             "migration_s": round(t, 6),
             "nvlink_gbs_per_gpu": round(max(rb["ingress"].values(), default=0) / t / 1e9, 2),
-            "roofline": {"bound": "nvlink", "achieved": round(achieved, 1), "peak": NVLINK_PEER_GBS, "unit": "GB/s",
-                         "frac": round(achieved / NVLINK_PEER_GBS, 4),
-                         "peak_source": "measured peer copy per direction per GPU on this pool (900 GB/s nominal)",
+            "roofline": {"bound": "nvlink", "achieved": round(achieved, 1), "peak": NVLINK_GBS, "unit": "GB/s",
+                         "frac": round(achieved / NVLINK_GBS, 4),
+                         "peak_source": "NVLink 5, 900 GB/s per direction per GPU",
+                         "frac_of_measured_peer_copy": round(achieved / NVLINK_MEASURED_PEER_GBS, 4),
                          "traffic": None, "algorithmic_bytes_per_launch": int(max_dir), "kernel_ms": round(t * 1e3, 4)},
             "gpu_launches": args.steps * sum(rt_phase_counts),
             "per_rank": [{"rank": r, "kernel_ms": p[0], "remote_gb": round(p[1] / 1e9, 3), "local_gb": round(p[2] / 1e9, 3)}
@@ -472,10 +498,8 @@ def run_reference_nccl(args):
     ops = O.schedule(spl, tpl, minimum_est_peers=1)
     subfields = [(s, k == "meta", S.TORCH_DTYPE[k]) for s, k in S.SUBFIELDS]
     shapes = {n: m.shape for metas in tpl.layout.values() for n, m in metas.items()}
-    plan = M.Plan(spl, tpl, minimum_est_peers=1)
-    its = [2, 4, 4, 4]
-    rb = plan.rank_bytes(its)
-    moved_all = int(plan.op_array["numel"].sum()) * sum(its)
+    rb = rank_bytes_ops(ops)  # the reference's path loads no product code
+    moved_all = sum(o.numel for o in ops) * STATE_BYTES_PER_ELEM
     times = []
     with Clocks(local) as ck:
         for i in range(args.warmup + args.steps):
@@ -500,11 +524,11 @@ def run_reference_nccl(args):
         "metric": METRIC, "impl": "reference-nccl", "value": round(moved_all / t / 1e9, 2), "unit": "GB/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t * 1e3, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic (as the ours arm)",
-        "config": {"workload": f"{cfg.name}: {cfg.note}, full training state (bf16 param + fp32 master/m/v + step)",
-                   "path": "oracle/nccl_port.py: execute_param_transfer over NCCL P2P per tensor, cat/clone, cuda_gc"},
+        "config": workload_config(cfg, world),
+        "path": "oracle/nccl_port.py: execute_param_transfer over NCCL P2P per tensor, cat/clone, cuda_gc",
         "migration_s": round(t, 6), "nvlink_gbs_per_gpu": round(max(rb["ingress"].values(), default=0) / t / 1e9, 2),
-        "roofline": {"bound": "nvlink", "achieved": round(max_dir / t / 1e9, 1), "peak": NVLINK_PEER_GBS, "unit": "GB/s",
-                     "frac": round(max_dir / t / 1e9 / NVLINK_PEER_GBS, 4)},
+        "roofline": {"bound": "nvlink", "achieved": round(max_dir / t / 1e9, 1), "peak": NVLINK_GBS, "unit": "GB/s",
+                     "frac": round(max_dir / t / 1e9 / NVLINK_GBS, 4)},
         "per_rank_ms": per_rank, "clocks": ck.summary(),
     }
 
@@ -620,8 +644,8 @@ def run_reference(args, world):
     return {
         "metric": METRIC, "value": round(v, 4), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(t / args.steps * 1e3, 3), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "u8", "data": "synthetic (seeded)", "impl": "reference",
-        "config": {"workload": f"{cfg.name}: {cfg.note} (bounded sample: {smp.what})"},
+        "dtype": "u8", "data": "synthetic (seeded N(0,0.02) weights, norms 1.0, m~N(0,1e-3), v~|N(0,1e-6)|)", "impl": "reference",
+        "config": workload_config(cfg, world),
         "cpu_baseline": {"value": round(v, 4), "unit": "GB/s", "cores": threads, "kind": "port", "sample": smp.describe(args.steps)},
         "e2e": {"value": round(v, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -655,7 +679,16 @@ def main():
                     help="N > 1, push: DP-replica fan-out (suika_b200.fanout); the default workloads have no replicas")
     ap.add_argument("--direction", choices=["pull", "push"], default="push",
                     help="N > 1: target ranks read their pieces (pull) or source ranks write them (push)")
+    ap.add_argument("--peer-probe", action="store_true",
+                    help="time the copy kernel's peer patterns between GPU 0 and GPU 1 instead (one process, 2 GPUs)")
+    ap.add_argument("--peer-gib", type=float, default=2.0)
+    ap.add_argument("--peer-variants", default="2,6")
+    ap.add_argument("--peer-one", action="store_true",
+                    help="with --peer-probe: one pull launch then one push launch on GPU 0 against GPU 1 (for a profiler)")
     args = ap.parse_args()
+    if args.peer_probe:
+        run_peer_probe(args)
+        return
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -710,6 +743,100 @@ def main():
     if res is not None:
         print(json.dumps(res), flush=True)
 
+
+
+# ---------------------------------------------------------------------------------------------
+# --peer-probe: peer patterns between two GPUs (one process)
+# ---------------------------------------------------------------------------------------------
+def _peer_enable_access() -> None:
+    import ctypes
+    import glob
+    libs = glob.glob(os.path.join(os.path.dirname(torch.__file__), "..", "nvidia", "cuda_runtime", "lib", "libcudart.so*"))
+    if not libs:
+        raise RuntimeError("libcudart not found next to torch")
+    rt = ctypes.CDLL(libs[0])
+    for a, b in ((0, 1), (1, 0)):
+        rt.cudaSetDevice(a)
+        rt.cudaDeviceEnablePeerAccess(b, 0)  # an "already enabled" return is fine
+
+
+def _peer_row(src, dst, n, strided, remote):
+    if strided:
+        return (src, dst, n // 2560, 1280, 2560, 2560, remote)
+    return (src, dst, 1, n, n, n, remote)
+
+
+def _peer_time(per_dev, reps=5):
+    preps = {}
+    for dev, ents in per_dev.items():
+        with torch.cuda.device(dev):
+            t = np.array([_peer_row(*e) for e in ents], dtype=M.L.COPY_DESC_DTYPE)
+            preps[dev] = M.PreparedCopies(t, torch.device("cuda", dev))
+    for dev, p in preps.items():
+        with torch.cuda.device(dev):
+            p.launch()
+    for d in (0, 1):
+        torch.cuda.synchronize(d)
+    ev = {}
+    for dev, p in preps.items():
+        with torch.cuda.device(dev):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for _ in range(reps):
+                p.launch()
+            b.record()
+            ev[dev] = (a, b)
+    for d in (0, 1):
+        torch.cuda.synchronize(d)
+    for p in preps.values():
+        p.check()
+    return max(a.elapsed_time(b) for a, b in ev.values()) / reps
+
+
+def run_peer_probe(args):
+    """Peer-bandwidth patterns between GPU 0 and GPU 1 for the copy kernel (one process). For each
+    launch shape (SUIKA_RS_VARIANT) and piece shape (one contiguous run; 1280-byte rows at a
+    2560-byte pitch, like a TP8 -> TP4 row-parallel piece) it times, per direction:
+      pull: the kernel on GPU a reads GPU b's memory;  push: it writes GPU b's memory;
+      1-way: one GPU copies;  2-way: both copy at once in opposite directions;
+      +local: the same table also holds an equal local copy (interleaved with the remote one).
+    These are the patterns a reshard is made of; they decide its direction and phasing."""
+    if torch.cuda.device_count() < 2:
+        raise SystemExit("needs two GPUs")
+    _peer_enable_access()
+    n = int(args.peer_gib * (1 << 30))
+    if args.peer_one:
+        d0, d1 = torch.device("cuda", 0), torch.device("cuda", 1)
+        a0, b0 = torch.ones(n, dtype=torch.uint8, device=d0), torch.empty(n, dtype=torch.uint8, device=d0)
+        a1 = torch.full((n,), 2, dtype=torch.uint8, device=d1)
+        b1 = torch.empty(n, dtype=torch.uint8, device=d1)
+        for name, (s_, d_) in (("pull", (a1, b0)), ("push", (a0, b1))):
+            p = M.PreparedCopies(np.array([_peer_row(s_.data_ptr(), d_.data_ptr(), n, False, 1)], dtype=M.L.COPY_DESC_DTYPE), d0)
+            p.launch()
+            p.check()
+            assert torch.equal(d_[:1024].cpu(), s_[:1024].cpu())
+            print(f"{name}: {n} bytes copied", flush=True)
+        return
+    b = {d: [torch.empty(n, dtype=torch.uint8, device=torch.device("cuda", d)) for _ in range(4)] for d in (0, 1)}
+    p = {d: [t.data_ptr() for t in b[d]] for d in (0, 1)}
+    for var in args.peer_variants.split(","):
+        os.environ["SUIKA_RS_VARIANT"] = var
+        for st in (False, True):
+            moved = n // 2 if st else n
+            pats = {
+                "pull 1-way": {0: [(p[1][0], p[0][1], n, st, 1)]},
+                "pull 2-way": {0: [(p[1][0], p[0][1], n, st, 1)], 1: [(p[0][0], p[1][1], n, st, 1)]},
+                "push 1-way": {0: [(p[0][0], p[1][1], n, st, 1)]},
+                "push 2-way": {0: [(p[0][0], p[1][1], n, st, 1)], 1: [(p[1][0], p[0][1], n, st, 1)]},
+                "pull 2-way +local": {0: [(p[1][0], p[0][1], n, st, 1), (p[0][2], p[0][3], n, st, 0)],
+                                      1: [(p[0][0], p[1][1], n, st, 1), (p[1][2], p[1][3], n, st, 0)]},
+                "push 2-way +local": {0: [(p[0][0], p[1][1], n, st, 1), (p[0][2], p[0][3], n, st, 0)],
+                                      1: [(p[1][0], p[0][1], n, st, 1), (p[1][2], p[1][3], n, st, 0)]},
+            }
+            for name, cfg in pats.items():
+                ms = _peer_time(cfg)
+                print(f"variant {var} {'strided' if st else 'contig '} {name:18s}: {ms:7.3f} ms  "
+                      f"{moved / ms / 1e6:6.0f} GB/s per direction", flush=True)
 
 
 # ---------------------------------------------------------------------------------------------
@@ -956,9 +1083,10 @@ def run_activation(args):
                                f"{ACT_BATCH} x {ACT_SEQ} tokens, hidden {ACT_HIDDEN}, bf16",
                    "received_mb_per_step": round((fwd_bytes + bwd_bytes) / 1e6, 1),
                    "l2": "buffers reused each step; per-step bytes above L2 only at N >= 4"},
-        "roofline": {"bound": "nvlink", "achieved": round(max_dir / t / 1e9, 1), "peak": NVLINK_PEER_GBS, "unit": "GB/s",
-                     "frac": round(max_dir / t / 1e9 / NVLINK_PEER_GBS, 4), "algorithmic_bytes_per_step": int(max_dir),
-                     "peak_source": "measured peer copy per direction per GPU on this pool (900 GB/s nominal)", "traffic": None},
+        "roofline": {"bound": "nvlink", "achieved": round(max_dir / t / 1e9, 1), "peak": NVLINK_GBS, "unit": "GB/s",
+                     "frac": round(max_dir / t / 1e9 / NVLINK_GBS, 4), "algorithmic_bytes_per_step": int(max_dir),
+                     "peak_source": "NVLink 5, 900 GB/s per direction per GPU",
+                     "frac_of_measured_peer_copy": round(max_dir / t / 1e9 / NVLINK_MEASURED_PEER_GBS, 4), "traffic": None},
         "per_rank_ms": per_rank, "clocks": ck.summary(), "check": check,
     }
     if launches is not None:

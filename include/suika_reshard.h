@@ -105,7 +105,8 @@ typedef struct rs_plan rs_plan;
 typedef struct rs_program rs_program;
 
 const char* rs_last_error(void);
-/* 1.1 adds rs_copy_launch_noalloc, rs_act_plan and rs_act_resolve; the 1.0 entry points are unchanged. */
+/* 1.1 adds rs_copy_launch_noalloc, rs_act_plan and rs_act_resolve; 1.2 adds rs_copy_run_bounded.
+ * The 1.0 entry points are unchanged. */
 int rs_version(int32_t* major, int32_t* minor);
 
 /* ---- planning: schedule_param_transfer (migration.py:322-381) -------------------------- */
@@ -277,8 +278,19 @@ int rs_copy_stage(const rs_copy_desc* descs, int64_t n_desc, void* workspace_dev
 /* Launch the copy kernel over a staged table (asynchronous; may be repeated while the workspace
  * and every address in the table stay valid). Synchronise the stream before reading targets. */
 int rs_copy_run(const void* workspace_dev, const rs_launch_info* info, void* stream);
-/* Status bits of the last launch over a staged table (synchronises `stream`): 0 = no error;
- * 1 = a bounded wait inside the kernel ran out (the kernel stopped early; targets incomplete). */
+/* rs_copy_run with an explicit bound on every wait inside the kernel. The TMA launch shapes
+ * (SUIKA_RS_VARIANT 5-7) wait on shared-memory barriers for their bulk loads; each wait gives up
+ * after wait_limit_ns (rs_copy_run uses 2 s), sets status bit 1, drains the copies it issued
+ * (bounded again) and ends the CTA, so a stuck copy never hangs the GPU. The vector-copy shapes
+ * have no waits. flags: 0, or RS_RUN_STALL_FIRST_STAGE to test that error path (every CTA arms
+ * its first stage for bytes that no copy delivers, so that wait runs out; targets stay
+ * incomplete); that flag needs a TMA launch shape (else RS_ERR_ARG). */
+#define RS_RUN_STALL_FIRST_STAGE 1u
+int rs_copy_run_bounded(const void* workspace_dev, const rs_launch_info* info, void* stream,
+                        uint64_t wait_limit_ns, uint32_t flags);
+/* Status bits of the launches over a staged table since rs_copy_stage cleared them (synchronises
+ * `stream`): 0 = no error; 1 = a bounded wait inside the kernel ran out (the kernel stopped
+ * early; targets incomplete). */
 int rs_copy_status(const void* workspace_dev, const rs_launch_info* info, void* stream, uint32_t* status);
 /* rs_copy_stage + rs_copy_run. n_desc == 0 is a no-op. */
 int rs_copy_launch(const rs_copy_desc* descs, int64_t n_desc,
@@ -300,6 +312,9 @@ int rs_copy_launch(const rs_copy_desc* descs, int64_t n_desc,
  *   - Every call shares the one array and overwrites the entries it uses; nothing in it needs
  *     to start at zero. Calls on the same stream are ordered; calls that overlap on the GPU
  *     (different streams, or several threads) race on the array.
+ *   - It always runs a vector-copy launch shape (SUIKA_RS_VARIANT 1-4 or 8; a TMA variant
+ *     selects the default shape 2 instead). Those kernels contain no waits, so a launch cannot
+ *     stop early and there is no status word to read back.
  * Otherwise it behaves like rs_copy_launch: same descriptors, same kernel, asynchronous. */
 #define RS_NOALLOC_MAX_ENTRIES 16384
 int rs_copy_launch_noalloc(const rs_copy_desc* descs, int64_t n_desc, void* stream, rs_launch_info* info);

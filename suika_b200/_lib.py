@@ -33,6 +33,7 @@ RS_ORDER_SEMANTIC = 1
 RS_SRC_REFERENCE = 0
 RS_SRC_BALANCED = 1
 RS_NOALLOC_MAX_ENTRIES = 16384
+RS_RUN_STALL_FIRST_STAGE = 1
 
 
 class RsTensorMeta(C.Structure):
@@ -165,6 +166,7 @@ SIGNATURES = {
     "rs_copy_workspace_bytes": (C.c_int, [C.c_int64, C.POINTER(C.c_uint64)]),
     "rs_copy_stage": (C.c_int, [_P, C.c_int64, _P, C.c_uint64, _P, C.POINTER(RsLaunchInfo)]),
     "rs_copy_run": (C.c_int, [_P, C.POINTER(RsLaunchInfo), _P]),
+    "rs_copy_run_bounded": (C.c_int, [_P, C.POINTER(RsLaunchInfo), _P, C.c_uint64, C.c_uint32]),
     "rs_copy_status": (C.c_int, [_P, C.POINTER(RsLaunchInfo), _P, C.POINTER(C.c_uint32)]),
     "rs_copy_launch": (C.c_int, [_P, C.c_int64, _P, C.c_uint64, _P, C.POINTER(RsLaunchInfo)]),
     "rs_copy_launch_noalloc": (C.c_int, [_P, C.c_int64, _P, C.POINTER(RsLaunchInfo)]),

@@ -276,10 +276,17 @@ struct Schedule {
   }
 };
 
+// Launch arguments every copy kernel takes. The vector-copy kernels use only the first four.
+struct RunArgs {
+  uint64_t wait_limit_ns;  // bound of every mbarrier wait (TMA kernels)
+  uint32_t flags;          // RS_RUN_* bits (TMA kernels)
+  uint32_t* status;        // kStatus* bits, OR-ed by the kernel
+};
+
 template <int BLOCK, int U, int MINB, bool STREAM = false>
 __global__ void __launch_bounds__(BLOCK, MINB) rs_copy_kernel(const DevSeg* __restrict__ segs, int32_t nseg, uint64_t ntiles,
-                                                               uint64_t nremote, uint32_t* status) {
-  (void)status;  // the vector-copy kernel has no waits that could fail
+                                                               uint64_t nremote, RunArgs run) {
+  (void)run;  // the vector-copy kernel has no waits that could fail
   Schedule sch;
   sch.init(segs, nseg, ntiles, nremote);
   Tile x;
@@ -307,7 +314,7 @@ __global__ void __launch_bounds__(BLOCK, MINB) rs_copy_kernel(const DevSeg* __re
 // sets kStatusWaitTimeout in *status, drains what it issued (bounded again) and stops.
 // ---------------------------------------------------------------------------------------------
 constexpr uint32_t kStatusWaitTimeout = 1u;
-constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s, the default bound of every wait
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 __device__ __forceinline__ uint64_t global_ns() {
@@ -328,11 +335,11 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t phase) {
       : "=r"(ok) : "r"(bar), "r"(phase) : "memory");
   return ok != 0;
 }
-__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t phase) {
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t phase, uint64_t limit_ns) {
   if (mbar_try_wait(bar, phase)) return true;
   const uint64_t t0 = global_ns();
   while (!mbar_try_wait(bar, phase))
-    if (global_ns() - t0 > kWaitLimitNs) return false;
+    if (global_ns() - t0 > limit_ns) return false;
   return true;
 }
 __device__ __forceinline__ void bulk_load(uint32_t smem_dst, const void* gsrc, uint32_t bytes, uint32_t bar) {
@@ -368,9 +375,9 @@ struct TmaPipe {
   uint32_t filled = 0;   // stages issued
   uint32_t retired = 0;  // stages stored
   bool failed = false;
-  uint32_t* status;
+  const RunArgs& run;
 
-  __device__ TmaPipe(Smem& s, uint32_t* st) : sm(s), status(st) {}
+  __device__ TmaPipe(Smem& s, const RunArgs& r) : sm(s), run(r) {}
 
   __device__ uint32_t cur() const { return filled % STAGES; }
 
@@ -402,8 +409,11 @@ struct TmaPipe {
     bulk_wait_read<STAGES - LOOKAHEAD>();
     const uint32_t bar = smem_u32(&sm.bar[s]);
     mbar_arrive_expect_tx(bar, sm.bytes[s]);
+    // RS_RUN_STALL_FIRST_STAGE (tests of the error path): the first stage's barrier expects bytes
+    // that no copy delivers, so its bounded wait runs out. No load is in flight into that stage.
+    const bool stall = (run.flags & RS_RUN_STALL_FIRST_STAGE) && filled == 0;
     const uint32_t base = smem_u32(&sm.buf[s][0]);
-    for (uint32_t i = 0; i < sm.count[s]; ++i) {
+    for (uint32_t i = 0; i < sm.count[s] && !stall; ++i) {
       const auto& e = sm.ent[s][i];
       bulk_load(base + e.off, reinterpret_cast<const void*>(e.src), e.bytes, bar);
     }
@@ -416,8 +426,8 @@ struct TmaPipe {
   __device__ void retire() {
     const uint32_t s = retired % STAGES;
     const uint32_t phase = (retired / STAGES) & 1u;
-    if (!mbar_wait_bounded(smem_u32(&sm.bar[s]), phase)) {
-      atomicOr(status, kStatusWaitTimeout);
+    if (!mbar_wait_bounded(smem_u32(&sm.bar[s]), phase, run.wait_limit_ns)) {
+      atomicOr(run.status, kStatusWaitTimeout);
       failed = true;
       return;
     }
@@ -436,7 +446,7 @@ struct TmaPipe {
     while (!failed && retired < filled) retire();
     if (failed) {  // drain the loads still in flight (bounded) before the CTA's shared memory goes away
       for (uint32_t q = retired + 1; q < filled; ++q)
-        (void)mbar_wait_bounded(smem_u32(&sm.bar[q % STAGES]), (q / STAGES) & 1u);
+        (void)mbar_wait_bounded(smem_u32(&sm.bar[q % STAGES]), (q / STAGES) & 1u, run.wait_limit_ns);
     }
     bulk_wait_all();
   }
@@ -444,7 +454,7 @@ struct TmaPipe {
 
 template <int STAGES, int STAGE_BYTES, int MAXE, int LOOKAHEAD, int MINB>
 __global__ void __launch_bounds__(32, MINB) rs_copy_tma_kernel(const DevSeg* __restrict__ segs, int32_t nseg, uint64_t ntiles,
-                                                               uint64_t nremote, uint32_t* status) {
+                                                               uint64_t nremote, RunArgs run) {
   using Pipe = TmaPipe<STAGES, STAGE_BYTES, MAXE, LOOKAHEAD>;
   extern __shared__ __align__(128) unsigned char smem_raw[];
   auto& sm = *reinterpret_cast<typename Pipe::Smem*>(smem_raw);
@@ -458,7 +468,7 @@ __global__ void __launch_bounds__(32, MINB) rs_copy_tma_kernel(const DevSeg* __r
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncwarp();
-  Pipe pipe(sm, status);
+  Pipe pipe(sm, run);
   Schedule sch;
   sch.init(segs, nseg, ntiles, nremote);
   Tile x;
@@ -486,7 +496,7 @@ __global__ void __launch_bounds__(32, MINB) rs_copy_tma_kernel(const DevSeg* __r
 struct Variant {
   int block, unroll, min_blocks;
   size_t smem;
-  void (*fn)(const DevSeg*, int32_t, uint64_t, uint64_t, uint32_t*);
+  void (*fn)(const DevSeg*, int32_t, uint64_t, uint64_t, RunArgs);
 };
 using TmaA = TmaSmem<8, 16384, 32>;
 using TmaB = TmaSmem<6, 16384, 32>;
@@ -620,18 +630,30 @@ int rs_copy_stage(const rs_copy_desc* descs, int64_t n_desc, void* workspace_dev
   return RS_OK;
 }
 
-int rs_copy_run(const void* workspace_dev, const rs_launch_info* info, void* stream) {
+int rs_copy_run_bounded(const void* workspace_dev, const rs_launch_info* info, void* stream, uint64_t wait_limit_ns,
+                        uint32_t flags) {
   if (!info) return efail(RS_ERR_ARG, "rs_copy_run: info is NULL");
   if (info->n_entries == 0 || info->n_tiles == 0) return RS_OK;
   if (!workspace_dev || info->grid <= 0 || info->variant < 0 || info->variant >= kNumVariants)
     return efail(RS_ERR_ARG, "rs_copy_run: info does not come from rs_copy_stage");
+  if (wait_limit_ns == 0) return efail(RS_ERR_ARG, "rs_copy_run_bounded: the wait limit must be positive");
+  if (flags & ~(uint32_t)RS_RUN_STALL_FIRST_STAGE) return efail(RS_ERR_ARG, "rs_copy_run_bounded: unknown flag bits");
   const Variant& v = kVariants[info->variant];
-  uint32_t* status = reinterpret_cast<uint32_t*>(static_cast<char*>(const_cast<void*>(workspace_dev)) + status_offset(info->n_entries));
+  if ((flags & RS_RUN_STALL_FIRST_STAGE) && v.smem == 0)
+    return efail(RS_ERR_ARG, "rs_copy_run_bounded: RS_RUN_STALL_FIRST_STAGE needs a TMA launch shape (SUIKA_RS_VARIANT 5-7)");
+  RunArgs run;
+  run.wait_limit_ns = wait_limit_ns;
+  run.flags = flags;
+  run.status = reinterpret_cast<uint32_t*>(static_cast<char*>(const_cast<void*>(workspace_dev)) + status_offset(info->n_entries));
   v.fn<<<(unsigned)info->grid, v.block, v.smem, reinterpret_cast<cudaStream_t>(stream)>>>(
-      reinterpret_cast<const DevSeg*>(workspace_dev), (int32_t)info->n_entries, info->n_tiles, info->n_tiles_remote, status);
+      reinterpret_cast<const DevSeg*>(workspace_dev), (int32_t)info->n_entries, info->n_tiles, info->n_tiles_remote, run);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "rs_copy_run: kernel launch");
   return RS_OK;
+}
+
+int rs_copy_run(const void* workspace_dev, const rs_launch_info* info, void* stream) {
+  return rs_copy_run_bounded(workspace_dev, info, stream, kWaitLimitNs, 0);
 }
 
 int rs_copy_status(const void* workspace_dev, const rs_launch_info* info, void* stream, uint32_t* status) {
@@ -749,13 +771,10 @@ namespace {
 // Every GPU that loads this library holds this array (RS_NOALLOC_MAX_ENTRIES x 72 bytes, about
 // 1.2 MB) until the process exits. All calls share it.
 static __device__ __align__(256) DevSeg g_noalloc_table[RS_NOALLOC_MAX_ENTRIES];
-// Status word of the last no-allocation launch (same bits as the workspace status block).
-static __device__ uint32_t g_noalloc_status;
 
 constexpr int kMaxDevices = 64;
 // Device address of g_noalloc_table per device ordinal, set once by the first call on that device.
 DevSeg* g_noalloc_addr[kMaxDevices] = {nullptr};
-uint32_t* g_noalloc_status_addr[kMaxDevices] = {nullptr};
 std::mutex g_noalloc_mu;
 
 int noalloc_table_addr(int dev, DevSeg** out) {
@@ -765,16 +784,20 @@ int noalloc_table_addr(int dev, DevSeg** out) {
     // In host code the array's name is only a stand-in; the device address has to be looked up,
     // with the device current.
     void* p = nullptr;
-    void* q = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_table);
     if (e != cudaSuccess) return cuda_fail(e, "rs_copy_launch_noalloc: cudaGetSymbolAddress");
-    e = cudaGetSymbolAddress(&q, g_noalloc_status);
-    if (e != cudaSuccess) return cuda_fail(e, "rs_copy_launch_noalloc: cudaGetSymbolAddress");
     g_noalloc_addr[dev] = static_cast<DevSeg*>(p);
-    g_noalloc_status_addr[dev] = static_cast<uint32_t*>(q);
   }
   *out = g_noalloc_addr[dev];
   return RS_OK;
+}
+
+// The no-allocation launch runs only the vector-copy kernels: they have no waits, so there is no
+// status a caller would have to read back. A TMA variant selected by SUIKA_RS_VARIANT falls back
+// to the default launch shape.
+int noalloc_variant() {
+  const int v = (int)std::min<uint64_t>(env_u64("SUIKA_RS_VARIANT", 2) - 1, kNumVariants - 1);
+  return kVariants[v].smem == 0 ? v : 1;
 }
 
 }  // namespace
@@ -788,7 +811,7 @@ int rs_copy_launch_noalloc(const rs_copy_desc* descs, int64_t n_desc, void* stre
   if (n_desc < 0 || (n_desc > 0 && !descs)) return efail(RS_ERR_ARG, "rs_copy_launch_noalloc: bad descriptor array");
   int64_t n_entries = 0;
   for (int64_t i = 0; i < n_desc; ++i)
-    if (descs[i].rows != 0 && descs[i].row_bytes != 0) ++n_entries;
+    if (!empty_desc(descs[i])) ++n_entries;
   if (n_entries > RS_NOALLOC_MAX_ENTRIES)
     return efail(RS_ERR_CAPACITY, "rs_copy_launch_noalloc: " + std::to_string(n_entries) + " non-empty copies, at most " +
                                       std::to_string(RS_NOALLOC_MAX_ENTRIES) + " fit the built-in table; use rs_copy_launch");
@@ -800,7 +823,7 @@ int rs_copy_launch_noalloc(const rs_copy_desc* descs, int64_t n_desc, void* stre
   int rc = noalloc_table_addr(dev, &table);
   if (rc) return rc;
   const uint64_t tile_bytes = std::min<uint64_t>(1ull << 30, std::max<uint64_t>(256, env_u64("SUIKA_RS_TILE_BYTES", kDefaultTileBytes))) & ~15ull;
-  const int variant = (int)std::min<uint64_t>(env_u64("SUIKA_RS_VARIANT", 2) - 1, kNumVariants - 1);
+  const int variant = noalloc_variant();
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   // Stage in chunks through a stack buffer: no heap memory on the host either. Pageable copies
   // are taken out of the buffer before cudaMemcpyAsync returns, so the buffer can be refilled.
@@ -814,10 +837,11 @@ int rs_copy_launch_noalloc(const rs_copy_desc* descs, int64_t n_desc, void* stre
     for (int64_t i = 0; i < n_desc; ++i) {
       const rs_copy_desc& d = descs[i];
       if (empty_desc(d) || remote_desc(d) != (pass == 0)) continue;
+      if (written + nc >= n_entries) return efail(RS_ERR_ARG, "rs_copy_launch_noalloc: descriptor count changed while staging");
       rc = make_entry(d, i, tile_bytes, ntiles, chunk[nc++], "rs_copy_launch_noalloc");
       if (rc) return rc;
       total += d.rows * d.row_bytes;
-      if (nc == kChunk || written + nc == n_entries) {
+      if (nc == kChunk) {
         e = cudaMemcpyAsync(table + written, chunk, nc * sizeof(DevSeg), cudaMemcpyHostToDevice, st);
         if (e != cudaSuccess) return cuda_fail(e, "rs_copy_launch_noalloc: staging the copy table");
         written += nc;
@@ -826,14 +850,15 @@ int rs_copy_launch_noalloc(const rs_copy_desc* descs, int64_t n_desc, void* stre
     }
     if (pass == 0) nremote = ntiles;
   }
+  if (nc > 0) {
+    e = cudaMemcpyAsync(table + written, chunk, nc * sizeof(DevSeg), cudaMemcpyHostToDevice, st);
+    if (e != cudaSuccess) return cuda_fail(e, "rs_copy_launch_noalloc: staging the copy table");
+    written += nc;
+  }
+  if (written != n_entries) return efail(RS_ERR_ARG, "rs_copy_launch_noalloc: staged entry count differs from the count");
   int sms = 0, per_sm = 0;
   const Variant& v = kVariants[variant];
-  uint32_t* status = g_noalloc_status_addr[dev];
-  if ((e = cudaMemsetAsync(status, 0, sizeof(uint32_t), st)) != cudaSuccess) return cuda_fail(e, "rs_copy_launch_noalloc: clearing status");
   if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
-  if (v.smem > 0 &&
-      (e = cudaFuncSetAttribute(v.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)v.smem)) != cudaSuccess)
-    return cuda_fail(e, "rs_copy_launch_noalloc: cudaFuncSetAttribute");
   if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, v.fn, v.block, v.smem)) != cudaSuccess)
     return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
   per_sm = (int)std::min<uint64_t>((uint64_t)std::max(per_sm, 1), env_u64("SUIKA_RS_CTAS_PER_SM", 8));
@@ -844,7 +869,12 @@ int rs_copy_launch_noalloc(const rs_copy_desc* descs, int64_t n_desc, void* stre
   li->variant = variant;
   li->grid = (int32_t)std::min<uint64_t>(ntiles, (uint64_t)sms * (uint64_t)per_sm);
   li->block = v.block;
-  v.fn<<<(unsigned)li->grid, v.block, v.smem, st>>>(table, (int32_t)n_entries, ntiles, nremote, status);
+  // The vector-copy kernels have no waits and never write a status word.
+  RunArgs run;
+  run.wait_limit_ns = kWaitLimitNs;
+  run.flags = 0;
+  run.status = nullptr;
+  v.fn<<<(unsigned)li->grid, v.block, 0, st>>>(table, (int32_t)n_entries, ntiles, nremote, run);
   if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(e, "rs_copy_launch_noalloc: kernel launch");
   return RS_OK;
 }

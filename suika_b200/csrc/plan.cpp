@@ -353,7 +353,7 @@ void rs_plan_free(rs_plan* plan) { delete plan; }
 
 int rs_version(int32_t* major, int32_t* minor) {
   if (major) *major = 1;
-  if (minor) *minor = 1;
+  if (minor) *minor = 2;
   return RS_OK;
 }
 

@@ -54,7 +54,7 @@ class TensorMeta:
             else:
                 self.shape = tensor.shape
         else:
-            assert dtype is not None and shape is not None, "Either tensor or (dtype, shape) should be provided"
+            assert dtype is not None and shape is not None, "a TensorMeta needs a tensor, or both a dtype and a shape"
         self.name = name
         if dtype is not None:
             self.dtype = dtype
@@ -110,7 +110,7 @@ class TensorMeta:
     __hash__ = None  # like the reference's class, which defines __eq__ only
 
     def __repr__(self) -> str:
-        return f"TensorMeta(name={self.name}, {self.dtype}, {self.shape}, {self.tp_meta})"
+        return f"<TensorMeta {self.name}: {self.dtype} full shape {tuple(self.shape)} tp_meta {self.tp_meta}>"
 
     __str__ = __repr__
 

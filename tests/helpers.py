@@ -115,3 +115,15 @@ class Memory:
             s = self.view(int(d["src_dev"]), (rows - 1) * sp + rb)
             t = self.view(int(d["dst_dev"]), (rows - 1) * dp + rb)
             copy_rect(t, 0, dp, s, 0, sp, rows, rb)
+
+
+def rank_device(rank: int, world: int):
+    """(device, process-group backend) of one rank of a multi-process GPU test. With a GPU per rank:
+    cuda:rank and NCCL. With fewer GPUs than ranks every rank shares cuda:0 and the process group
+    is gloo (NCCL refuses two ranks on one device). CUDA IPC between processes works on one device
+    too, and no kernel of this package waits on another rank, so the ranks' kernels may run in any
+    order on the shared GPU."""
+    import torch
+    if torch.cuda.device_count() >= world:
+        return torch.device("cuda", rank), "nccl"
+    return torch.device("cuda", 0), "gloo"

@@ -130,6 +130,50 @@ def test_copy_kernel_random_rectangles(tile, variant, monkeypatch):
     assert torch.equal(dst, want)
 
 
+@pytest.mark.parametrize("variant", ["5", "6", "7"])
+def test_tma_wait_that_runs_out_reports_status_and_returns(variant, monkeypatch):
+    """The bounded-wait error path of the TMA launch shapes, made to happen without a fault: every
+    CTA arms its first stage's barrier for bytes that no copy delivers (RS_RUN_STALL_FIRST_STAGE),
+    with a 1 ms limit. The wait runs out, the kernel drains what it issued and returns, and the
+    status word reads 1. The context stays usable: the same table, staged again and run normally,
+    then copies correctly with status 0."""
+    import ctypes as C
+    monkeypatch.setenv("SUIKA_RS_VARIANT", variant)
+    lib = M.L.load()
+    src = torch.randint(0, 255, (32 << 20,), dtype=torch.uint8, device=DEV)
+    dst = torch.zeros_like(src)
+    rows, rb, pitch = 2048, 4096, 8192  # 16-byte aligned rows: all of them go through the bulk copies
+    table = np.array([(src.data_ptr() + h * rb, dst.data_ptr() + h * rb, rows, rb, pitch, pitch, 0) for h in (0, 1)],
+                     dtype=M.L.COPY_DESC_DTYPE)
+    prepared = M.PreparedCopies(table, DEV)
+    stream = C.c_void_p(torch.cuda.current_stream(DEV).cuda_stream)
+    M.L.check(lib.rs_copy_run_bounded(prepared.workspace.data_ptr(), C.byref(prepared.info), stream, 1_000_000,
+                                      M.L.RS_RUN_STALL_FIRST_STAGE))
+    torch.cuda.synchronize()
+    assert prepared.status() == 1
+    with pytest.raises(M.L.ReshardError):
+        prepared.check()
+    assert not torch.equal(dst, src)  # the stalled stages were never copied
+    again = M.PreparedCopies(table, DEV)  # staging clears the status block
+    again.launch()
+    torch.cuda.synchronize()
+    assert again.status() == 0
+    assert torch.equal(dst, src)
+
+
+def test_stall_flag_needs_a_tma_shape(monkeypatch):
+    import ctypes as C
+    monkeypatch.setenv("SUIKA_RS_VARIANT", "2")
+    lib = M.L.load()
+    buf = torch.zeros(1 << 16, dtype=torch.uint8, device=DEV)
+    table = np.array([(buf.data_ptr(), buf.data_ptr() + 32768, 1, 4096, 4096, 4096, 0)], dtype=M.L.COPY_DESC_DTYPE)
+    prepared = M.PreparedCopies(table, DEV)
+    rc = lib.rs_copy_run_bounded(prepared.workspace.data_ptr(), C.byref(prepared.info), None, 1_000_000,
+                                 M.L.RS_RUN_STALL_FIRST_STAGE)
+    assert rc == M.L.RS_ERR_ARG and b"TMA" in lib.rs_last_error()
+    assert lib.rs_copy_run_bounded(prepared.workspace.data_ptr(), C.byref(prepared.info), None, 0, 0) == M.L.RS_ERR_ARG
+
+
 def test_empty_table_is_a_noop():
     info = M.launch_copies(np.zeros(0, dtype=M.L.COPY_DESC_DTYPE), DEV)
     assert info.n_tiles == 0
