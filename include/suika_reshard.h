@@ -265,11 +265,20 @@ typedef struct rs_launch_info {
                               with local tiles so NVLink and HBM copies overlap) */
   int32_t grid;            /* CTAs launched                            */
   int32_t block;           /* threads per CTA                          */
-  int32_t variant;         /* launch shape (SUIKA_RS_VARIANT, 1-based) */
+  int32_t variant;         /* launch shape (SUIKA_RS_VARIANT - 1)      */
   int32_t reserved;
+  /* Tensor-map launch shapes (SUIKA_RS_VARIANT 9-12): the local, 16-byte aligned entries go to a
+   * kernel that moves 2-D boxes with cp.async.bulk.tensor (one load and one store per box of up
+   * to 2 KB x rows); the fields above then describe the other entries, run by the vector copy. */
+  int64_t n_tensor_entries; /* entries (tensor-map pairs) of the tensor-map kernel */
+  uint64_t n_tensor_tiles;  /* boxes it moves                                      */
+  int32_t tensor_grid;      /* its CTAs                                             */
+  int32_t tensor_block;     /* its threads per CTA                                  */
 } rs_launch_info;
 
-/* Device workspace the caller must provide to rs_copy_stage / rs_copy_launch for n descriptors. */
+/* Device workspace the caller must provide to rs_copy_stage / rs_copy_launch for n descriptors
+ * (256-byte aligned). It depends on the launch shape SUIKA_RS_VARIANT selects at the time of the
+ * call (the tensor-map shapes also stage two 128-byte tensor maps per entry). */
 int rs_copy_workspace_bytes(int64_t n_desc, uint64_t* bytes);
 /* Cut the table into tiles and stage it into workspace_dev (stream-ordered copy on `stream`, a
  * cudaStream_t; NULL = legacy default stream). Fills *info for rs_copy_run. */

@@ -105,7 +105,9 @@ class RsCopyDesc(C.Structure):
 
 class RsLaunchInfo(C.Structure):
     _fields_ = [("n_tiles", C.c_uint64), ("total_bytes", C.c_uint64), ("n_entries", C.c_int64), ("n_tiles_remote", C.c_uint64),
-                ("grid", C.c_int32), ("block", C.c_int32), ("variant", C.c_int32), ("reserved", C.c_int32)]
+                ("grid", C.c_int32), ("block", C.c_int32), ("variant", C.c_int32), ("reserved", C.c_int32),
+                ("n_tensor_entries", C.c_int64), ("n_tensor_tiles", C.c_uint64), ("tensor_grid", C.c_int32),
+                ("tensor_block", C.c_int32)]
 
 
 class RsPeerHandle(C.Structure):

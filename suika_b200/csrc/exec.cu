@@ -489,6 +489,143 @@ __global__ void __launch_bounds__(32, MINB) rs_copy_tma_kernel(const DevSeg* __r
   if (leader) pipe.finish();
 }
 
+// ---------------------------------------------------------------------------------------------
+// Tensor-map variant: 2-D TMA boxes through a shared-memory ring (SUIKA_RS_VARIANT 9-12).
+// Every local, 16-byte aligned entry is described to the TMA unit as two 2-D tensors of 8-byte
+// elements, its source and its target, each (row_bytes / 8) x rows with its own pitch; one
+// cp.async.bulk.tensor.2d load moves a box of up to 2 KB x box_h rows (a whole strided tile) into
+// a shared-memory stage, and one cp.async.bulk.tensor.2d store writes it to the target. The TMA
+// unit clips boxes at the tensor edges, so ragged tiles need no code. One thread per CTA issues
+// everything; STAGES - 1 loads stay in flight behind the store being issued. Entries that do not
+// qualify (remote, or not 16-byte aligned) are left to the vector-copy kernel in the same run.
+// Tensor maps never describe another GPU's memory here and no load uses cluster multicast.
+// ---------------------------------------------------------------------------------------------
+struct alignas(64) TensorEntry {
+  CUtensorMap src;      // 2-D map of the source: (row_bytes / 8, rows), pitch = source pitch
+  CUtensorMap dst;      // 2-D map of the target: (row_bytes / 8, rows), pitch = target pitch
+  uint64_t tile_begin;  // global index of this entry's first box
+  uint32_t col_boxes;   // boxes across a row
+  uint32_t box_w;       // box width in 8-byte elements (even: x * 8 stays 16-byte aligned)
+  uint32_t box_h;       // box height in rows
+  uint32_t box_bytes;   // box_w * 8 * box_h: the bytes a box load always delivers to shared memory
+};
+static_assert(sizeof(TensorEntry) == 320, "TensorEntry layout");
+
+__device__ __forceinline__ void tma_load_2d(uint32_t smem_dst, const CUtensorMap* map, int32_t x, int32_t y, uint32_t bar) {
+  asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+               ::"r"(smem_dst), "l"(map), "r"(x), "r"(y), "r"(bar) : "memory");
+}
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, int32_t x, int32_t y, uint32_t smem_src) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%1, %2}], [%3];"
+               ::"l"(map), "r"(x), "r"(y), "r"(smem_src) : "memory");
+}
+// The maps were written to global memory by a host copy before the launch; acquire them for the
+// tensor-map proxy before their first use.
+__device__ __forceinline__ void tensormap_acquire(const CUtensorMap* map) {
+  asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(map) : "memory");
+}
+
+struct TensorCursor {
+  int32_t si;
+  uint64_t next_begin;
+  __device__ void init(const TensorEntry* __restrict__ ents, int32_t n, uint64_t t) {
+    int32_t lo = 0, hi = n - 1;
+    while (lo < hi) {
+      const int32_t mid = (lo + hi + 1) >> 1;
+      if (ents[mid].tile_begin <= t) lo = mid; else hi = mid - 1;
+    }
+    si = lo;
+    next_begin = (si + 1 < n) ? ents[si + 1].tile_begin : ~0ull;
+  }
+  __device__ const TensorEntry& locate(const TensorEntry* __restrict__ ents, int32_t n, uint64_t t) {
+    while (t >= next_begin) {
+      ++si;
+      next_begin = (si + 1 < n) ? ents[si + 1].tile_begin : ~0ull;
+    }
+    return ents[si];
+  }
+};
+
+template <int STAGES, int STAGE_BYTES>
+constexpr size_t tensor_smem_bytes() {
+  return (size_t)STAGES * STAGE_BYTES + 1024 + (size_t)STAGES * (8 + 16);
+}
+
+template <int STAGES, int STAGE_BYTES>
+__global__ void __launch_bounds__(32, 1) rs_copy_tensor_kernel(const TensorEntry* __restrict__ ents, int32_t nent, uint64_t ntiles,
+                                                               RunArgs run) {
+  extern __shared__ unsigned char smem_raw[];
+  if (threadIdx.x != 0) return;
+  struct Slot {
+    const CUtensorMap* dst;
+    int32_t x, y;
+  };
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;  // stage buffers start 1 KB aligned
+  unsigned char* gbase = smem_raw + (base - raw);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(gbase + (size_t)STAGES * STAGE_BYTES);
+  Slot* slots = reinterpret_cast<Slot*>(bars + STAGES);
+  for (int s = 0; s < STAGES; ++s) mbar_init(smem_u32(&bars[s]), 1);
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+
+  const uint64_t b = blockIdx.x, g = gridDim.x;
+  const uint64_t n = ntiles > b ? (ntiles - b + g - 1) / g : 0;
+  if (n == 0) return;
+  TensorCursor cur;
+  cur.init(ents, nent, b);
+  int32_t acquired = -1;
+  uint64_t issued = 0;
+  const bool stall_first = (run.flags & RS_RUN_STALL_FIRST_STAGE) != 0;
+  auto issue = [&]() {
+    const uint64_t t = b + issued * g;
+    const TensorEntry& e = cur.locate(ents, nent, t);
+    if (cur.si != acquired) {
+      tensormap_acquire(&e.src);
+      tensormap_acquire(&e.dst);
+      acquired = cur.si;
+    }
+    const uint32_t cb_all = e.col_boxes;
+    const uint32_t lt = (uint32_t)(t - e.tile_begin);
+    const uint32_t rb = lt / cb_all, cb = lt - rb * cb_all;
+    const uint32_t s = (uint32_t)(issued % STAGES);
+    Slot& sl = slots[s];
+    sl.dst = &e.dst;
+    sl.x = (int32_t)(cb * e.box_w);
+    sl.y = (int32_t)(rb * e.box_h);
+    const uint32_t bar = smem_u32(&bars[s]);
+    mbar_arrive_expect_tx(bar, e.box_bytes);
+    // RS_RUN_STALL_FIRST_STAGE (tests of the error path): the first box's barrier expects bytes
+    // that no load delivers, so its bounded wait runs out; nothing is in flight into that stage.
+    if (!(stall_first && issued == 0)) tma_load_2d(base + s * (uint32_t)STAGE_BYTES, &e.src, sl.x, sl.y, bar);
+    ++issued;
+  };
+  const uint64_t prologue = n < (uint64_t)(STAGES - 1) ? n : (uint64_t)(STAGES - 1);
+  while (issued < prologue) issue();
+  uint64_t k = 0;
+  bool failed = false;
+  for (; k < n; ++k) {
+    const uint32_t s = (uint32_t)(k % STAGES);
+    if (!mbar_wait_bounded(smem_u32(&bars[s]), (uint32_t)(k / STAGES) & 1u, run.wait_limit_ns)) {
+      failed = true;
+      break;
+    }
+    tma_store_2d(slots[s].dst, slots[s].x, slots[s].y, base + s * (uint32_t)STAGE_BYTES);
+    bulk_commit();
+    if (issued < n) {
+      // the new box goes into the stage of box k - 1, whose store must have read it out
+      bulk_wait_read<1>();
+      issue();
+    }
+  }
+  if (failed) {
+    atomicOr(run.status, kStatusWaitTimeout);
+    // loads that may still be in flight into shared memory (at most STAGES - 1, one per stage)
+    for (uint64_t q = k; q < issued; ++q)
+      (void)mbar_wait_bounded(smem_u32(&bars[q % STAGES]), (uint32_t)(q / STAGES) & 1u, run.wait_limit_ns);
+  }
+  bulk_wait_all();
+}
+
 // Launch shapes. Vector-copy variants: (threads per CTA, 16-byte loads in flight per thread, CTAs
 // per SM), each with 64 KB of loads in flight per SM; on cfg2b (1 x B200, 128 KB tiles) they span
 // 5.83-6.00 TB/s. TMA variants: one warp per CTA, (stages, stage bytes, stages in flight, CTAs per
@@ -512,10 +649,28 @@ const Variant kVariants[] = {
     {256, 8, 2, 0, rs_copy_kernel<256, 8, 2, true>},  // 8: variant 2 with streaming cache hints
 };
 constexpr int kNumVariants = sizeof(kVariants) / sizeof(kVariants[0]);
+constexpr int kTensorVectorVariant = 1;  // launch shape of the entries the tensor-map kernel leaves out
 
-// Workspace layout: the staged table, then a 256-byte status block (word 0: kStatus* bits).
+// Tensor-map launch shapes (SUIKA_RS_VARIANT 9-12): (stages, stage bytes); one warp per CTA, CTAs
+// per SM as shared memory allows (1 for about 192 KB of stages, 2 for about 96 KB).
+struct TensorShape {
+  int stages, stage_bytes;
+  size_t smem;
+  void (*fn)(const TensorEntry*, int32_t, uint64_t, RunArgs);
+};
+const TensorShape kTensorShapes[] = {
+    {8, 24576, tensor_smem_bytes<8, 24576>(), rs_copy_tensor_kernel<8, 24576>},
+    {4, 24576, tensor_smem_bytes<4, 24576>(), rs_copy_tensor_kernel<4, 24576>},
+    {4, 49152, tensor_smem_bytes<4, 49152>(), rs_copy_tensor_kernel<4, 49152>},
+    {6, 16384, tensor_smem_bytes<6, 16384>(), rs_copy_tensor_kernel<6, 16384>},
+};
+constexpr int kNumTensorShapes = sizeof(kTensorShapes) / sizeof(kTensorShapes[0]);
+
+// Workspace layout: the staged vector-copy table, a 256-byte status block (word 0: kStatus* bits),
+// then, for the tensor-map shapes, the TensorEntry table.
 constexpr uint64_t kStatusBytes = 256;
 uint64_t status_offset(int64_t n_entries) { return ((uint64_t)n_entries * sizeof(DevSeg) + 255) & ~255ull; }
+uint64_t tensor_offset(int64_t n_entries) { return status_offset(n_entries) + kStatusBytes; }
 
 uint64_t env_u64(const char* name, uint64_t dflt) {
   const char* v = std::getenv(name);
@@ -523,6 +678,33 @@ uint64_t env_u64(const char* name, uint64_t dflt) {
   char* end = nullptr;
   const unsigned long long x = std::strtoull(v, &end, 10);
   return (end && *end == 0 && x > 0) ? (uint64_t)x : dflt;
+}
+
+// Launch shape chosen by SUIKA_RS_VARIANT (1-based; default 2): 0-based index below kNumVariants
+// for the vector and bulk-copy kernels, kNumVariants + i for tensor-map shape i.
+int selected_variant() {
+  return (int)std::min<uint64_t>(env_u64("SUIKA_RS_VARIANT", 2) - 1, kNumVariants + kNumTensorShapes - 1);
+}
+bool is_tensor_variant(int v) { return v >= kNumVariants; }
+
+// cuTensorMapEncodeTiled, looked up once through the runtime (no link against libcuda).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*, const cuuint64_t*,
+                                  const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+int encode_tiled_fn(EncodeTiledFn* out) {
+  static EncodeTiledFn fn = nullptr;
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !p)
+      return efail(RS_ERR_CUDA, "rs_copy_stage: cuTensorMapEncodeTiled entry point unavailable");
+    fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  *out = fn;
+  return RS_OK;
 }
 
 // Largest power of two <= 16 dividing every address, pitch and row length of the entry.
@@ -567,6 +749,68 @@ int make_entry(const rs_copy_desc& d, int64_t i, uint64_t tile_bytes, uint64_t& 
 bool empty_desc(const rs_copy_desc& d) { return d.rows == 0 || d.row_bytes == 0; }
 bool remote_desc(const rs_copy_desc& d) { return (d.flags & RS_COPY_REMOTE) != 0; }
 
+// An entry the tensor-map kernel takes: this GPU's memory on both sides, 16-byte aligned addresses
+// and pitches (the TMA rules for a tensor's base and strides), whole 8-byte elements per row.
+bool tensor_desc(const rs_copy_desc& d) {
+  if (remote_desc(d) || (d.src_dev | d.dst_dev) & 15 || d.row_bytes & 7) return false;
+  if (d.rows > 1 && ((d.src_pitch | d.dst_pitch) & 15)) return false;
+  return d.rows < (1ull << 31) && d.row_bytes / 8 <= (1ull << 32);
+}
+
+int encode_2d(EncodeTiledFn fn, CUtensorMap* m, uint64_t addr, uint64_t cols, uint64_t rows, uint64_t pitch, uint32_t bw,
+              uint32_t bh) {
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {pitch};
+  const cuuint32_t box[2] = {bw, bh};
+  const cuuint32_t elem_strides[2] = {1, 1};
+  const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, reinterpret_cast<void*>(addr), dims, strides, box, elem_strides,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return efail(RS_ERR_CUDA, "rs_copy_stage: cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+  return RS_OK;
+}
+
+// One rows x row_bytes rectangle -> one TensorEntry, its boxes numbered from `ntiles`. Boxes are
+// as wide as a row allows up to 2 KB (widths split evenly, even element counts) and as tall as
+// the stage holds.
+int add_tensor_entry(EncodeTiledFn fn, uint64_t src, uint64_t dst, uint64_t rows, uint64_t row_bytes, uint64_t sp, uint64_t dp,
+                     uint32_t stage_bytes, uint64_t& ntiles, std::vector<TensorEntry>& out) {
+  const uint64_t cols = row_bytes / 8;
+  const uint64_t nbx = (cols + 255) / 256;
+  uint64_t bw = (cols + nbx - 1) / nbx;
+  bw += bw & 1;
+  const uint64_t bh = std::min<uint64_t>(std::min<uint64_t>(rows, 256), std::max<uint64_t>(1, stage_bytes / (bw * 8)));
+  if (rows == 1) sp = dp = (row_bytes + 15) & ~15ull;  // one row: the stride only has to be legal
+  TensorEntry te;
+  std::memset(&te, 0, sizeof(te));
+  te.col_boxes = (uint32_t)((cols + bw - 1) / bw);
+  te.box_w = (uint32_t)bw;
+  te.box_h = (uint32_t)bh;
+  te.box_bytes = (uint32_t)(bw * 8 * bh);
+  te.tile_begin = ntiles;
+  int rc = encode_2d(fn, &te.src, src, cols, rows, sp, (uint32_t)bw, (uint32_t)bh);
+  if (!rc) rc = encode_2d(fn, &te.dst, dst, cols, rows, dp, (uint32_t)bw, (uint32_t)bh);
+  if (rc) return rc;
+  ntiles += (uint64_t)te.col_boxes * ((rows + bh - 1) / bh);
+  out.push_back(te);
+  return RS_OK;
+}
+
+// A descriptor -> tensor entries. A contiguous run (one row, or pitches equal to the row) is seen
+// as 2 KB rows plus a shorter last row, so its boxes are full-width.
+int make_tensor_entries(EncodeTiledFn fn, const rs_copy_desc& d, uint32_t stage_bytes, uint64_t& ntiles,
+                        std::vector<TensorEntry>& out) {
+  const bool contiguous = d.rows == 1 || (d.src_pitch == d.row_bytes && d.dst_pitch == d.row_bytes);
+  const uint64_t total = d.rows * d.row_bytes;
+  if (contiguous && total >= 4096) {
+    const uint64_t w = 2048, main_rows = total / w, rem = total % w;
+    int rc = add_tensor_entry(fn, d.src_dev, d.dst_dev, main_rows, w, w, w, stage_bytes, ntiles, out);
+    if (!rc && rem) rc = add_tensor_entry(fn, d.src_dev + main_rows * w, d.dst_dev + main_rows * w, 1, rem, rem, rem, stage_bytes, ntiles, out);
+    return rc;
+  }
+  return add_tensor_entry(fn, d.src_dev, d.dst_dev, d.rows, d.row_bytes, d.src_pitch, d.dst_pitch, stage_bytes, ntiles, out);
+}
+
 }  // namespace
 
 extern "C" {
@@ -574,6 +818,7 @@ extern "C" {
 int rs_copy_workspace_bytes(int64_t n_desc, uint64_t* bytes) {
   if (!bytes || n_desc < 0) return efail(RS_ERR_ARG, "rs_copy_workspace_bytes: bad argument");
   *bytes = (((uint64_t)n_desc * sizeof(DevSeg) + 255) & ~255ull) + kStatusBytes;
+  if (is_tensor_variant(selected_variant())) *bytes += 2 * (uint64_t)n_desc * sizeof(TensorEntry);  // a run may become 2 entries
   return RS_OK;
 }
 
@@ -583,18 +828,31 @@ int rs_copy_stage(const rs_copy_desc* descs, int64_t n_desc, void* workspace_dev
   std::memset(info, 0, sizeof(*info));
   if (n_desc < 0 || (n_desc > 0 && !descs)) return efail(RS_ERR_ARG, "rs_copy_stage: bad descriptor array");
   const uint64_t tile_bytes = std::min<uint64_t>(1ull << 30, std::max<uint64_t>(256, env_u64("SUIKA_RS_TILE_BYTES", kDefaultTileBytes))) & ~15ull;
-  const int variant = (int)std::min<uint64_t>(env_u64("SUIKA_RS_VARIANT", 2) - 1, kNumVariants - 1);  // env value 1-based
+  const int variant = selected_variant();
+  const bool tensor = is_tensor_variant(variant);
+  EncodeTiledFn encode = nullptr;
+  if (tensor) {
+    const int rc = encode_tiled_fn(&encode);
+    if (rc) return rc;
+  }
   std::vector<DevSeg> table;
+  std::vector<TensorEntry> tensor_table;
   table.reserve((size_t)n_desc);
-  uint64_t ntiles = 0, total = 0, nremote = 0;
+  uint64_t ntiles = 0, total = 0, nremote = 0, ntensor_tiles = 0;
   for (int pass = 0; pass < 2; ++pass) {  // remote entries first, then local ones
     for (int64_t i = 0; i < n_desc; ++i) {
       const rs_copy_desc& d = descs[i];
       if (empty_desc(d) || remote_desc(d) != (pass == 0)) continue;
       DevSeg sg;
-      const int rc = make_entry(d, i, tile_bytes, ntiles, sg, "rs_copy_stage");
+      int rc = make_entry(d, i, tile_bytes, ntiles, sg, "rs_copy_stage");  // validates the descriptor either way
       if (rc) return rc;
       total += d.rows * d.row_bytes;
+      if (tensor && tensor_desc(d)) {
+        ntiles = sg.tile_begin;  // not a vector-copy entry after all
+        rc = make_tensor_entries(encode, d, (uint32_t)kTensorShapes[variant - kNumVariants].stage_bytes, ntensor_tiles, tensor_table);
+        if (rc) return rc;
+        continue;
+      }
       table.push_back(sg);
     }
     if (pass == 0) nremote = ntiles;
@@ -604,51 +862,92 @@ int rs_copy_stage(const rs_copy_desc* descs, int64_t n_desc, void* workspace_dev
   info->n_tiles_remote = nremote;
   info->total_bytes = total;
   info->variant = variant;
-  if (table.empty()) return RS_OK;
-  if (table.size() > 0x7fffffffull) return efail(RS_ERR_ARG, "rs_copy_stage: too many entries");
-  const uint64_t need = status_offset((int64_t)table.size()) + kStatusBytes;
+  info->n_tensor_entries = (int64_t)tensor_table.size();
+  info->n_tensor_tiles = ntensor_tiles;
+  if (table.empty() && tensor_table.empty()) return RS_OK;
+  if (table.size() > 0x7fffffffull || tensor_table.size() > 0x7fffffffull) return efail(RS_ERR_ARG, "rs_copy_stage: too many entries");
+  const uint64_t need = tensor_offset((int64_t)table.size()) + tensor_table.size() * sizeof(TensorEntry);
   if (!workspace_dev || workspace_bytes < need)
     return efail(RS_ERR_CAPACITY, "rs_copy_stage: workspace of " + std::to_string(workspace_bytes) + " bytes, need " + std::to_string(need));
+  if (reinterpret_cast<uintptr_t>(workspace_dev) & 255) return efail(RS_ERR_ARG, "rs_copy_stage: workspace must be 256-byte aligned");
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   // Pageable source: the runtime copies the table out before returning, so it may be freed.
-  cudaError_t e = cudaMemcpyAsync(workspace_dev, table.data(), table.size() * sizeof(DevSeg), cudaMemcpyHostToDevice, st);
-  if (e != cudaSuccess) return cuda_fail(e, "rs_copy_stage: staging the copy table");
+  cudaError_t e = cudaSuccess;
+  if (!table.empty()) {
+    e = cudaMemcpyAsync(workspace_dev, table.data(), table.size() * sizeof(DevSeg), cudaMemcpyHostToDevice, st);
+    if (e != cudaSuccess) return cuda_fail(e, "rs_copy_stage: staging the copy table");
+  }
+  if (!tensor_table.empty()) {
+    e = cudaMemcpyAsync(static_cast<char*>(workspace_dev) + tensor_offset((int64_t)table.size()), tensor_table.data(),
+                        tensor_table.size() * sizeof(TensorEntry), cudaMemcpyHostToDevice, st);
+    if (e != cudaSuccess) return cuda_fail(e, "rs_copy_stage: staging the tensor maps");
+  }
   e = cudaMemsetAsync(static_cast<char*>(workspace_dev) + status_offset((int64_t)table.size()), 0, kStatusBytes, st);
   if (e != cudaSuccess) return cuda_fail(e, "rs_copy_stage: clearing the status block");
   int dev = 0, sms = 0, per_sm = 0;
-  const Variant& v = kVariants[variant];
   if ((e = cudaGetDevice(&dev)) != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
-  if (v.smem > 0 &&
-      (e = cudaFuncSetAttribute(v.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)v.smem)) != cudaSuccess)
-    return cuda_fail(e, "rs_copy_stage: cudaFuncSetAttribute");
-  if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, v.fn, v.block, v.smem)) != cudaSuccess)
-    return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
-  per_sm = (int)std::min<uint64_t>((uint64_t)std::max(per_sm, 1), env_u64("SUIKA_RS_CTAS_PER_SM", 8));
-  info->grid = (int32_t)std::min<uint64_t>(ntiles, (uint64_t)sms * (uint64_t)per_sm);
-  info->block = v.block;
+  const uint64_t cap_per_sm = env_u64("SUIKA_RS_CTAS_PER_SM", 8);
+  const Variant& v = kVariants[tensor ? kTensorVectorVariant : variant];
+  if (!table.empty()) {
+    if (v.smem > 0 &&
+        (e = cudaFuncSetAttribute(v.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)v.smem)) != cudaSuccess)
+      return cuda_fail(e, "rs_copy_stage: cudaFuncSetAttribute");
+    if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, v.fn, v.block, v.smem)) != cudaSuccess)
+      return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+    per_sm = (int)std::min<uint64_t>((uint64_t)std::max(per_sm, 1), cap_per_sm);
+    info->grid = (int32_t)std::min<uint64_t>(ntiles, (uint64_t)sms * (uint64_t)per_sm);
+    info->block = v.block;
+  }
+  if (!tensor_table.empty()) {
+    const TensorShape& ts = kTensorShapes[variant - kNumVariants];
+    if ((e = cudaFuncSetAttribute(ts.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ts.smem)) != cudaSuccess)
+      return cuda_fail(e, "rs_copy_stage: cudaFuncSetAttribute (tensor-map kernel)");
+    if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, ts.fn, 32, ts.smem)) != cudaSuccess)
+      return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+    per_sm = (int)std::min<uint64_t>((uint64_t)std::max(per_sm, 1), cap_per_sm);
+    info->tensor_grid = (int32_t)std::min<uint64_t>(ntensor_tiles, (uint64_t)sms * (uint64_t)per_sm);
+    info->tensor_block = 32;
+  }
   return RS_OK;
 }
 
 int rs_copy_run_bounded(const void* workspace_dev, const rs_launch_info* info, void* stream, uint64_t wait_limit_ns,
                         uint32_t flags) {
   if (!info) return efail(RS_ERR_ARG, "rs_copy_run: info is NULL");
-  if (info->n_entries == 0 || info->n_tiles == 0) return RS_OK;
-  if (!workspace_dev || info->grid <= 0 || info->variant < 0 || info->variant >= kNumVariants)
+  const bool vec_part = info->n_entries > 0 && info->n_tiles > 0;
+  const bool tensor_part = info->n_tensor_entries > 0 && info->n_tensor_tiles > 0;
+  if (!vec_part && !tensor_part) return RS_OK;
+  if (!workspace_dev || info->variant < 0 || info->variant >= kNumVariants + kNumTensorShapes || (vec_part && info->grid <= 0) ||
+      (tensor_part && (info->tensor_grid <= 0 || !is_tensor_variant(info->variant))))
     return efail(RS_ERR_ARG, "rs_copy_run: info does not come from rs_copy_stage");
   if (wait_limit_ns == 0) return efail(RS_ERR_ARG, "rs_copy_run_bounded: the wait limit must be positive");
   if (flags & ~(uint32_t)RS_RUN_STALL_FIRST_STAGE) return efail(RS_ERR_ARG, "rs_copy_run_bounded: unknown flag bits");
-  const Variant& v = kVariants[info->variant];
-  if ((flags & RS_RUN_STALL_FIRST_STAGE) && v.smem == 0)
-    return efail(RS_ERR_ARG, "rs_copy_run_bounded: RS_RUN_STALL_FIRST_STAGE needs a TMA launch shape (SUIKA_RS_VARIANT 5-7)");
+  const bool tensor = is_tensor_variant(info->variant);
+  const Variant& v = kVariants[tensor ? kTensorVectorVariant : info->variant];
+  if ((flags & RS_RUN_STALL_FIRST_STAGE) && !(tensor ? tensor_part : v.smem > 0))
+    return efail(RS_ERR_ARG, "rs_copy_run_bounded: RS_RUN_STALL_FIRST_STAGE needs a TMA launch shape (SUIKA_RS_VARIANT 5-7 or 9-12)");
+  char* ws = static_cast<char*>(const_cast<void*>(workspace_dev));
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   RunArgs run;
   run.wait_limit_ns = wait_limit_ns;
   run.flags = flags;
-  run.status = reinterpret_cast<uint32_t*>(static_cast<char*>(const_cast<void*>(workspace_dev)) + status_offset(info->n_entries));
-  v.fn<<<(unsigned)info->grid, v.block, v.smem, reinterpret_cast<cudaStream_t>(stream)>>>(
-      reinterpret_cast<const DevSeg*>(workspace_dev), (int32_t)info->n_entries, info->n_tiles, info->n_tiles_remote, run);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "rs_copy_run: kernel launch");
+  run.status = reinterpret_cast<uint32_t*>(ws + status_offset(info->n_entries));
+  if (vec_part) {
+    RunArgs vrun = run;
+    if (tensor) vrun.flags = 0;  // the stall hook is meant for the tensor-map kernel
+    v.fn<<<(unsigned)info->grid, v.block, v.smem, st>>>(reinterpret_cast<const DevSeg*>(ws), (int32_t)info->n_entries, info->n_tiles,
+                                                        info->n_tiles_remote, vrun);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "rs_copy_run: kernel launch");
+  }
+  if (tensor_part) {
+    const TensorShape& ts = kTensorShapes[info->variant - kNumVariants];
+    ts.fn<<<(unsigned)info->tensor_grid, 32, ts.smem, st>>>(reinterpret_cast<const TensorEntry*>(ws + tensor_offset(info->n_entries)),
+                                                           (int32_t)info->n_tensor_entries, info->n_tensor_tiles, run);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "rs_copy_run: tensor-map kernel launch");
+  }
   return RS_OK;
 }
 
@@ -659,7 +958,7 @@ int rs_copy_run(const void* workspace_dev, const rs_launch_info* info, void* str
 int rs_copy_status(const void* workspace_dev, const rs_launch_info* info, void* stream, uint32_t* status) {
   if (!info || !status) return efail(RS_ERR_ARG, "rs_copy_status: NULL argument");
   *status = 0;
-  if (info->n_entries == 0) return RS_OK;
+  if (info->n_entries == 0 && info->n_tensor_entries == 0) return RS_OK;
   if (!workspace_dev) return efail(RS_ERR_ARG, "rs_copy_status: NULL workspace");
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   uint32_t v = 0;
@@ -796,8 +1095,8 @@ int noalloc_table_addr(int dev, DevSeg** out) {
 // status a caller would have to read back. A TMA variant selected by SUIKA_RS_VARIANT falls back
 // to the default launch shape.
 int noalloc_variant() {
-  const int v = (int)std::min<uint64_t>(env_u64("SUIKA_RS_VARIANT", 2) - 1, kNumVariants - 1);
-  return kVariants[v].smem == 0 ? v : 1;
+  const int v = selected_variant();
+  return (!is_tensor_variant(v) && kVariants[v].smem == 0) ? v : 1;
 }
 
 }  // namespace

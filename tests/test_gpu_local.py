@@ -94,7 +94,7 @@ def test_views_move_only_row_split_pieces():
     assert info.total_bytes == moved + 4 * len([1 for r in (0, 1) for _ in out[r]])  # + one 4-byte step per tensor
 
 
-@pytest.mark.parametrize("variant", ["1", "2", "3", "4", "5", "6", "7", "8"])
+@pytest.mark.parametrize("variant", ["1", "2", "3", "4", "5", "6", "7", "8", "9", "10", "11", "12"])
 @pytest.mark.parametrize("tile", ["256", "4096", "131072"])
 def test_copy_kernel_random_rectangles(tile, variant, monkeypatch):
     """Strided copies with random alignment, pitch and size (every vector width, column-split rows),
@@ -140,9 +140,9 @@ def test_tma_wait_that_runs_out_reports_status_and_returns(variant, monkeypatch)
     import ctypes as C
     monkeypatch.setenv("SUIKA_RS_VARIANT", variant)
     lib = M.L.load()
-    src = torch.randint(0, 255, (32 << 20,), dtype=torch.uint8, device=DEV)
-    dst = torch.zeros_like(src)
     rows, rb, pitch = 2048, 4096, 8192  # 16-byte aligned rows: all of them go through the bulk copies
+    src = torch.randint(0, 255, (rows * pitch,), dtype=torch.uint8, device=DEV)  # the two halves cover every byte
+    dst = torch.zeros_like(src)
     table = np.array([(src.data_ptr() + h * rb, dst.data_ptr() + h * rb, rows, rb, pitch, pitch, 0) for h in (0, 1)],
                      dtype=M.L.COPY_DESC_DTYPE)
     prepared = M.PreparedCopies(table, DEV)
@@ -172,6 +172,81 @@ def test_stall_flag_needs_a_tma_shape(monkeypatch):
                                  M.L.RS_RUN_STALL_FIRST_STAGE)
     assert rc == M.L.RS_ERR_ARG and b"TMA" in lib.rs_last_error()
     assert lib.rs_copy_run_bounded(prepared.workspace.data_ptr(), C.byref(prepared.info), None, 0, 0) == M.L.RS_ERR_ARG
+
+
+@pytest.mark.parametrize("variant", ["9", "10", "11", "12"])
+def test_tensor_map_kernel_edges(variant, monkeypatch):
+    """The 2-D tensor-map kernel on the geometry its boxes have to clip: rows narrower than a box,
+    widths that are not a multiple of the box width (odd element counts), row counts that leave a
+    partial last box, one-row runs, and long contiguous runs cut into 2 KB rows plus a remainder.
+    Every entry is local and 16-byte aligned, so all of them go to the tensor-map kernel."""
+    monkeypatch.setenv("SUIKA_RS_VARIANT", variant)
+    g = torch.Generator(device=DEV).manual_seed(int(variant))
+    src = torch.randint(0, 255, (48 << 20,), dtype=torch.uint8, device=DEV, generator=g)
+    dst = torch.zeros(64 << 20, dtype=torch.uint8, device=DEV)
+    want = torch.zeros_like(dst)
+    shapes = [(1, 8, 16, 16), (3, 24, 32, 48), (17, 2056, 4096, 2064), (5, 4104, 8208, 4112), (1000, 11008, 22016, 11008),
+              (37, 1280, 2560, 1280), (1, 40000, 40000, 40000), (1, 4096 * 3 + 8, 0, 0), (64, 2048, 2048, 2048),
+              (250, 16, 32, 16), (300, 22016, 44032, 22016), (1, 2 << 20, 0, 0)]
+    descs, so, do = [], 0, 0
+    for rows, rb, sp, dp in shapes:
+        sp, dp = sp or rb, dp or rb
+        descs.append((src.data_ptr() + so, dst.data_ptr() + do, rows, rb, sp, dp, 0))
+        for r in range(rows):
+            want[do + r * dp: do + r * dp + rb] = src[so + r * sp: so + r * sp + rb]
+        so = (so + (rows - 1) * sp + rb + 4095) // 4096 * 4096 + 16
+        do = (do + (rows - 1) * dp + rb + 4095) // 4096 * 4096 + 32
+    assert so < src.numel() and do < dst.numel()
+    prepared = M.PreparedCopies(np.array(descs, dtype=M.L.COPY_DESC_DTYPE), DEV)
+    info = prepared.launch()
+    assert info.n_entries == 0 and info.n_tensor_entries >= len(shapes)  # contiguous runs may add a remainder entry
+    torch.cuda.synchronize()
+    assert prepared.status() == 0
+    assert torch.equal(dst, want)
+
+
+@pytest.mark.parametrize("variant", ["9", "10"])
+@pytest.mark.parametrize("case", ["cfg2b_mini", "cfg3_mini", "odd_mini", "qwen_grow_mini"])
+def test_reshard_local_tensor_map_shapes_match_reference(case, variant, monkeypatch):
+    """A whole reshard through the tensor-map launch shapes equals the reference's digests."""
+    monkeypatch.setenv("SUIKA_RS_VARIANT", variant)
+    g = load_golden(case)
+    cfg = CASES[case]["config"]
+    spl, tpl = cfg.layouts()
+    states = golden_states(cfg, seed=g["seed"])
+    out = M.reshard_local(spl, tpl, to_device(states), S.expected_sub_fields(), DEV,
+                          minimum_est_peers=g["minimum_est_peers"])
+    torch.cuda.synchronize()
+    for rank_s, want in g["ranks"].items():
+        got = out[int(rank_s)]
+        assert list(got) == want["order"]
+        for name, fields in want["digests"].items():
+            for sub, exp in fields.items():
+                t = got[name][sub]
+                assert [list(t.shape), str(t.dtype).replace("torch.", ""), digest(host(t))] == exp, (rank_s, name, sub)
+
+
+@pytest.mark.parametrize("variant", ["9", "12"])
+def test_tensor_map_wait_that_runs_out_reports_status(variant, monkeypatch):
+    """The bounded-wait error path of the tensor-map kernel (same hook as the bulk-copy shapes)."""
+    import ctypes as C
+    monkeypatch.setenv("SUIKA_RS_VARIANT", variant)
+    lib = M.L.load()
+    src = torch.randint(0, 255, (2048 * 8192,), dtype=torch.uint8, device=DEV)  # the two halves cover every byte
+    dst = torch.zeros_like(src)
+    table = np.array([(src.data_ptr() + h * 4096, dst.data_ptr() + h * 4096, 2048, 4096, 8192, 8192, 0) for h in (0, 1)],
+                     dtype=M.L.COPY_DESC_DTYPE)
+    prepared = M.PreparedCopies(table, DEV)
+    assert prepared.info.n_tensor_entries == 2
+    stream = C.c_void_p(torch.cuda.current_stream(DEV).cuda_stream)
+    M.L.check(lib.rs_copy_run_bounded(prepared.workspace.data_ptr(), C.byref(prepared.info), stream, 1_000_000,
+                                      M.L.RS_RUN_STALL_FIRST_STAGE))
+    torch.cuda.synchronize()
+    assert prepared.status() == 1
+    again = M.PreparedCopies(table, DEV)
+    again.launch()
+    torch.cuda.synchronize()
+    assert again.status() == 0 and torch.equal(dst, src)
 
 
 def test_empty_table_is_a_noop():
