@@ -267,7 +267,7 @@ typedef struct rs_launch_info {
   int32_t block;           /* threads per CTA                          */
   int32_t variant;         /* launch shape (SUIKA_RS_VARIANT - 1)      */
   int32_t reserved;
-  /* Tensor-map launch shapes (SUIKA_RS_VARIANT 9-12): the local, 16-byte aligned entries go to a
+  /* Tensor-map launch shapes (SUIKA_RS_VARIANT 9-14): the local, 16-byte aligned entries go to a
    * kernel that moves 2-D boxes with cp.async.bulk.tensor (one load and one store per box of up
    * to 2 KB x rows); the fields above then describe the other entries, run by the vector copy. */
   int64_t n_tensor_entries; /* entries (tensor-map pairs) of the tensor-map kernel */

@@ -490,7 +490,7 @@ __global__ void __launch_bounds__(32, MINB) rs_copy_tma_kernel(const DevSeg* __r
 }
 
 // ---------------------------------------------------------------------------------------------
-// Tensor-map variant: 2-D TMA boxes through a shared-memory ring (SUIKA_RS_VARIANT 9-12).
+// Tensor-map variant: 2-D TMA boxes through a shared-memory ring (SUIKA_RS_VARIANT 9-14).
 // Every local, 16-byte aligned entry is described to the TMA unit as two 2-D tensors of 8-byte
 // elements, its source and its target, each (row_bytes / 8) x rows with its own pitch; one
 // cp.async.bulk.tensor.2d load moves a box of up to 2 KB x box_h rows (a whole strided tile) into
@@ -518,6 +518,22 @@ __device__ __forceinline__ void tma_load_2d(uint32_t smem_dst, const CUtensorMap
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, int32_t x, int32_t y, uint32_t smem_src) {
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%1, %2}], [%3];"
                ::"l"(map), "r"(x), "r"(y), "r"(smem_src) : "memory");
+}
+// The same with an L2 cache policy (evict-first: every byte is read once and written once).
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ void tma_load_2d_hint(uint32_t smem_dst, const CUtensorMap* map, int32_t x, int32_t y, uint32_t bar,
+                                                 uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%2, %3}], [%4], %5;"
+      ::"r"(smem_dst), "l"(map), "r"(x), "r"(y), "r"(bar), "l"(policy) : "memory");
+}
+__device__ __forceinline__ void tma_store_2d_hint(const CUtensorMap* map, int32_t x, int32_t y, uint32_t smem_src, uint64_t policy) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group.L2::cache_hint [%0, {%1, %2}], [%3], %4;"
+               ::"l"(map), "r"(x), "r"(y), "r"(smem_src), "l"(policy) : "memory");
 }
 // The maps were written to global memory by a host copy before the launch; acquire them for the
 // tensor-map proxy before their first use.
@@ -551,7 +567,7 @@ constexpr size_t tensor_smem_bytes() {
   return (size_t)STAGES * STAGE_BYTES + 1024 + (size_t)STAGES * (8 + 16);
 }
 
-template <int STAGES, int STAGE_BYTES>
+template <int STAGES, int STAGE_BYTES, bool EVICT_FIRST>
 __global__ void __launch_bounds__(32, 1) rs_copy_tensor_kernel(const TensorEntry* __restrict__ ents, int32_t nent, uint64_t ntiles,
                                                                RunArgs run) {
   extern __shared__ unsigned char smem_raw[];
@@ -576,6 +592,7 @@ __global__ void __launch_bounds__(32, 1) rs_copy_tensor_kernel(const TensorEntry
   int32_t acquired = -1;
   uint64_t issued = 0;
   const bool stall_first = (run.flags & RS_RUN_STALL_FIRST_STAGE) != 0;
+  const uint64_t policy = EVICT_FIRST ? l2_evict_first_policy() : 0;
   auto issue = [&]() {
     const uint64_t t = b + issued * g;
     const TensorEntry& e = cur.locate(ents, nent, t);
@@ -596,7 +613,10 @@ __global__ void __launch_bounds__(32, 1) rs_copy_tensor_kernel(const TensorEntry
     mbar_arrive_expect_tx(bar, e.box_bytes);
     // RS_RUN_STALL_FIRST_STAGE (tests of the error path): the first box's barrier expects bytes
     // that no load delivers, so its bounded wait runs out; nothing is in flight into that stage.
-    if (!(stall_first && issued == 0)) tma_load_2d(base + s * (uint32_t)STAGE_BYTES, &e.src, sl.x, sl.y, bar);
+    if (!(stall_first && issued == 0)) {
+      if (EVICT_FIRST) tma_load_2d_hint(base + s * (uint32_t)STAGE_BYTES, &e.src, sl.x, sl.y, bar, policy);
+      else tma_load_2d(base + s * (uint32_t)STAGE_BYTES, &e.src, sl.x, sl.y, bar);
+    }
     ++issued;
   };
   const uint64_t prologue = n < (uint64_t)(STAGES - 1) ? n : (uint64_t)(STAGES - 1);
@@ -609,7 +629,8 @@ __global__ void __launch_bounds__(32, 1) rs_copy_tensor_kernel(const TensorEntry
       failed = true;
       break;
     }
-    tma_store_2d(slots[s].dst, slots[s].x, slots[s].y, base + s * (uint32_t)STAGE_BYTES);
+    if (EVICT_FIRST) tma_store_2d_hint(slots[s].dst, slots[s].x, slots[s].y, base + s * (uint32_t)STAGE_BYTES, policy);
+    else tma_store_2d(slots[s].dst, slots[s].x, slots[s].y, base + s * (uint32_t)STAGE_BYTES);
     bulk_commit();
     if (issued < n) {
       // the new box goes into the stage of box k - 1, whose store must have read it out
@@ -651,7 +672,7 @@ const Variant kVariants[] = {
 constexpr int kNumVariants = sizeof(kVariants) / sizeof(kVariants[0]);
 constexpr int kTensorVectorVariant = 1;  // launch shape of the entries the tensor-map kernel leaves out
 
-// Tensor-map launch shapes (SUIKA_RS_VARIANT 9-12): (stages, stage bytes); one warp per CTA, CTAs
+// Tensor-map launch shapes (SUIKA_RS_VARIANT 9-14): (stages, stage bytes, evict-first hints); one warp per CTA, CTAs
 // per SM as shared memory allows (1 for about 192 KB of stages, 2 for about 96 KB).
 struct TensorShape {
   int stages, stage_bytes;
@@ -659,10 +680,12 @@ struct TensorShape {
   void (*fn)(const TensorEntry*, int32_t, uint64_t, RunArgs);
 };
 const TensorShape kTensorShapes[] = {
-    {8, 24576, tensor_smem_bytes<8, 24576>(), rs_copy_tensor_kernel<8, 24576>},
-    {4, 24576, tensor_smem_bytes<4, 24576>(), rs_copy_tensor_kernel<4, 24576>},
-    {4, 49152, tensor_smem_bytes<4, 49152>(), rs_copy_tensor_kernel<4, 49152>},
-    {6, 16384, tensor_smem_bytes<6, 16384>(), rs_copy_tensor_kernel<6, 16384>},
+    {8, 24576, tensor_smem_bytes<8, 24576>(), rs_copy_tensor_kernel<8, 24576, false>},
+    {4, 24576, tensor_smem_bytes<4, 24576>(), rs_copy_tensor_kernel<4, 24576, false>},
+    {4, 49152, tensor_smem_bytes<4, 49152>(), rs_copy_tensor_kernel<4, 49152, false>},
+    {6, 16384, tensor_smem_bytes<6, 16384>(), rs_copy_tensor_kernel<6, 16384, false>},
+    {8, 24576, tensor_smem_bytes<8, 24576>(), rs_copy_tensor_kernel<8, 24576, true>},   // 13: 9 with evict-first L2 hints
+    {4, 49152, tensor_smem_bytes<4, 49152>(), rs_copy_tensor_kernel<4, 49152, true>},   // 14: 11 with evict-first L2 hints
 };
 constexpr int kNumTensorShapes = sizeof(kTensorShapes) / sizeof(kTensorShapes[0]);
 
@@ -771,13 +794,13 @@ int encode_2d(EncodeTiledFn fn, CUtensorMap* m, uint64_t addr, uint64_t cols, ui
 }
 
 // One rows x row_bytes rectangle -> one TensorEntry, its boxes numbered from `ntiles`. Boxes are
-// as wide as a row allows up to 2 KB (widths split evenly, even element counts) and as tall as
-// the stage holds.
+// 2 KB wide (256 elements; a narrower row gets one box as wide as the row, rounded up to an even
+// element count) so that every box but a row's last starts and ends on 128-byte lines, and as tall
+// as the stage holds.
 int add_tensor_entry(EncodeTiledFn fn, uint64_t src, uint64_t dst, uint64_t rows, uint64_t row_bytes, uint64_t sp, uint64_t dp,
                      uint32_t stage_bytes, uint64_t& ntiles, std::vector<TensorEntry>& out) {
   const uint64_t cols = row_bytes / 8;
-  const uint64_t nbx = (cols + 255) / 256;
-  uint64_t bw = (cols + nbx - 1) / nbx;
+  uint64_t bw = std::min<uint64_t>(cols, 256);
   bw += bw & 1;
   const uint64_t bh = std::min<uint64_t>(std::min<uint64_t>(rows, 256), std::max<uint64_t>(1, stage_bytes / (bw * 8)));
   if (rows == 1) sp = dp = (row_bytes + 15) & ~15ull;  // one row: the stride only has to be legal
@@ -926,7 +949,7 @@ int rs_copy_run_bounded(const void* workspace_dev, const rs_launch_info* info, v
   const bool tensor = is_tensor_variant(info->variant);
   const Variant& v = kVariants[tensor ? kTensorVectorVariant : info->variant];
   if ((flags & RS_RUN_STALL_FIRST_STAGE) && !(tensor ? tensor_part : v.smem > 0))
-    return efail(RS_ERR_ARG, "rs_copy_run_bounded: RS_RUN_STALL_FIRST_STAGE needs a TMA launch shape (SUIKA_RS_VARIANT 5-7 or 9-12)");
+    return efail(RS_ERR_ARG, "rs_copy_run_bounded: RS_RUN_STALL_FIRST_STAGE needs a TMA launch shape (SUIKA_RS_VARIANT 5-7 or 9-14)");
   char* ws = static_cast<char*>(const_cast<void*>(workspace_dev));
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   RunArgs run;

@@ -637,6 +637,7 @@ def reshard_local(source_param_layout, target_param_layout, source_state_dicts: 
                              np.array([t.numel() * t.element_size() for t in srcs], np.uint64),
                              np.array([t.data_ptr() for t in dst_t], np.uint64),
                              np.array([t.numel() * t.element_size() for t in dst_t], np.uint64))
+            d["flags"] &= ~np.uint64(L.RS_COPY_REMOTE)  # every rank is on this device: nothing crosses NVLink
             tables.append(d[keep])
         ent: Dict[str, Dict[str, torch.Tensor]] = {}
         for ds, t in zip(prog.dst_slots, dst_t):

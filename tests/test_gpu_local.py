@@ -94,7 +94,7 @@ def test_views_move_only_row_split_pieces():
     assert info.total_bytes == moved + 4 * len([1 for r in (0, 1) for _ in out[r]])  # + one 4-byte step per tensor
 
 
-@pytest.mark.parametrize("variant", ["1", "2", "3", "4", "5", "6", "7", "8", "9", "10", "11", "12"])
+@pytest.mark.parametrize("variant", ["1", "2", "3", "4", "5", "6", "7", "8", "9", "10", "11", "12", "13", "14"])
 @pytest.mark.parametrize("tile", ["256", "4096", "131072"])
 def test_copy_kernel_random_rectangles(tile, variant, monkeypatch):
     """Strided copies with random alignment, pitch and size (every vector width, column-split rows),
@@ -174,7 +174,7 @@ def test_stall_flag_needs_a_tma_shape(monkeypatch):
     assert lib.rs_copy_run_bounded(prepared.workspace.data_ptr(), C.byref(prepared.info), None, 0, 0) == M.L.RS_ERR_ARG
 
 
-@pytest.mark.parametrize("variant", ["9", "10", "11", "12"])
+@pytest.mark.parametrize("variant", ["9", "10", "11", "12", "13", "14"])
 def test_tensor_map_kernel_edges(variant, monkeypatch):
     """The 2-D tensor-map kernel on the geometry its boxes have to clip: rows narrower than a box,
     widths that are not a multiple of the box width (odd element counts), row counts that leave a
@@ -205,7 +205,7 @@ def test_tensor_map_kernel_edges(variant, monkeypatch):
     assert torch.equal(dst, want)
 
 
-@pytest.mark.parametrize("variant", ["9", "10"])
+@pytest.mark.parametrize("variant", ["9", "11", "14"])
 @pytest.mark.parametrize("case", ["cfg2b_mini", "cfg3_mini", "odd_mini", "qwen_grow_mini"])
 def test_reshard_local_tensor_map_shapes_match_reference(case, variant, monkeypatch):
     """A whole reshard through the tensor-map launch shapes equals the reference's digests."""
@@ -226,7 +226,7 @@ def test_reshard_local_tensor_map_shapes_match_reference(case, variant, monkeypa
                 assert [list(t.shape), str(t.dtype).replace("torch.", ""), digest(host(t))] == exp, (rank_s, name, sub)
 
 
-@pytest.mark.parametrize("variant", ["9", "12"])
+@pytest.mark.parametrize("variant", ["9", "12", "14"])
 def test_tensor_map_wait_that_runs_out_reports_status(variant, monkeypatch):
     """The bounded-wait error path of the tensor-map kernel (same hook as the bulk-copy shapes)."""
     import ctypes as C
