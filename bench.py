@@ -296,7 +296,10 @@ def run_single(args):
     check = verify_views(spl, tpl, state.state, out) if not args.no_check else {"status": "skipped"}
     moved = int(info.total_bytes)
     units = moved_bytes_views(plan, spl, tpl)
-    log(f"pack table: {info.n_entries} copies, {info.n_tiles} tiles, grid {info.grid}x{info.block} (variant {info.variant + 1}); "
+    launches_per_step = int(info.n_entries > 0) + int(info.n_tensor_entries > 0)
+    log(f"pack table: {info.n_entries} vector copies in {info.n_tiles} tiles (grid {info.grid}x{info.block}), "
+        f"{info.n_tensor_entries} tensor-map copies in {info.n_tensor_tiles} boxes (grid {info.tensor_grid}x{info.tensor_block}); "
+        f"launch shape {info.variant + 1}, {launches_per_step} kernel(s) per step; "
         f"{moved / 1e9:.2f} GB per step")
     with Clocks(0) as ck:
         for _ in range(args.warmup):
@@ -331,7 +334,7 @@ def run_single(args):
                      "frac": round(achieved / peak, 4), "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs, burst copy)",
                      "traffic": int(tpu * moved),
                      "algorithmic_bytes_per_launch": 2 * moved, "kernel_ms": round(kern_s * 1e3, 4)},
-        "gpu_launches": args.steps,
+        "gpu_launches": args.steps * launches_per_step,
         "clocks": ck.summary(),
         "check": check,
     }

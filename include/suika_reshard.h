@@ -281,7 +281,9 @@ typedef struct rs_launch_info {
  * call (the tensor-map shapes also stage two 128-byte tensor maps per entry). */
 int rs_copy_workspace_bytes(int64_t n_desc, uint64_t* bytes);
 /* Cut the table into tiles and stage it into workspace_dev (stream-ordered copy on `stream`, a
- * cudaStream_t; NULL = legacy default stream). Fills *info for rs_copy_run. */
+ * cudaStream_t; NULL = legacy default stream). Fills *info for rs_copy_run. The launch shape is
+ * SUIKA_RS_VARIANT's; unset, a table with no RS_COPY_REMOTE entry takes the tensor-map shape 11
+ * and any other table the vector shape 2. */
 int rs_copy_stage(const rs_copy_desc* descs, int64_t n_desc, void* workspace_dev, uint64_t workspace_bytes,
                   void* stream, rs_launch_info* info);
 /* Launch the copy kernel over a staged table (asynchronous; may be repeated while the workspace
@@ -321,9 +323,9 @@ int rs_copy_launch(const rs_copy_desc* descs, int64_t n_desc,
  *   - Every call shares the one array and overwrites the entries it uses; nothing in it needs
  *     to start at zero. Calls on the same stream are ordered; calls that overlap on the GPU
  *     (different streams, or several threads) race on the array.
- *   - It always runs a vector-copy launch shape (SUIKA_RS_VARIANT 1-4 or 8; a TMA variant
- *     selects the default shape 2 instead). Those kernels contain no waits, so a launch cannot
- *     stop early and there is no status word to read back.
+ *   - It always runs a vector-copy launch shape (SUIKA_RS_VARIANT 1-4 or 8; unset, or a TMA
+ *     shape, selects shape 2). Those kernels contain no waits, so a launch cannot stop early and
+ *     there is no status word to read back.
  * Otherwise it behaves like rs_copy_launch: same descriptors, same kernel, asynchronous. */
 #define RS_NOALLOC_MAX_ENTRIES 16384
 int rs_copy_launch_noalloc(const rs_copy_desc* descs, int64_t n_desc, void* stream, rs_launch_info* info);

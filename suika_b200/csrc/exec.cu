@@ -703,10 +703,18 @@ uint64_t env_u64(const char* name, uint64_t dflt) {
   return (end && *end == 0 && x > 0) ? (uint64_t)x : dflt;
 }
 
-// Launch shape chosen by SUIKA_RS_VARIANT (1-based; default 2): 0-based index below kNumVariants
-// for the vector and bulk-copy kernels, kNumVariants + i for tensor-map shape i.
+// Launch shape chosen by SUIKA_RS_VARIANT (1-based): 0-based index below kNumVariants for the
+// vector and bulk-copy kernels, kNumVariants + i for tensor-map shape i. Unset (or 0) selects per
+// table: a table whose entries all stay in this GPU's memory runs the tensor-map shape 11 (4 x 48
+// KB stages, the fastest on a one-GPU relayout); a table with any entry that crosses NVLink runs
+// the vector shape 2, whose CTAs interleave remote and local tiles so both links stay busy.
+constexpr int kAutoVariant = -1;
+constexpr int kAutoLocalVariant = kNumVariants + 2;
+constexpr int kAutoRemoteVariant = 1;
 int selected_variant() {
-  return (int)std::min<uint64_t>(env_u64("SUIKA_RS_VARIANT", 2) - 1, kNumVariants + kNumTensorShapes - 1);
+  const uint64_t v = env_u64("SUIKA_RS_VARIANT", 0);
+  if (v == 0) return kAutoVariant;
+  return (int)std::min<uint64_t>(v - 1, kNumVariants + kNumTensorShapes - 1);
 }
 bool is_tensor_variant(int v) { return v >= kNumVariants; }
 
@@ -841,7 +849,8 @@ extern "C" {
 int rs_copy_workspace_bytes(int64_t n_desc, uint64_t* bytes) {
   if (!bytes || n_desc < 0) return efail(RS_ERR_ARG, "rs_copy_workspace_bytes: bad argument");
   *bytes = (((uint64_t)n_desc * sizeof(DevSeg) + 255) & ~255ull) + kStatusBytes;
-  if (is_tensor_variant(selected_variant())) *bytes += 2 * (uint64_t)n_desc * sizeof(TensorEntry);  // a run may become 2 entries
+  const int v = selected_variant();
+  if (v == kAutoVariant || is_tensor_variant(v)) *bytes += 2 * (uint64_t)n_desc * sizeof(TensorEntry);  // a run may become 2 entries
   return RS_OK;
 }
 
@@ -851,13 +860,14 @@ int rs_copy_stage(const rs_copy_desc* descs, int64_t n_desc, void* workspace_dev
   std::memset(info, 0, sizeof(*info));
   if (n_desc < 0 || (n_desc > 0 && !descs)) return efail(RS_ERR_ARG, "rs_copy_stage: bad descriptor array");
   const uint64_t tile_bytes = std::min<uint64_t>(1ull << 30, std::max<uint64_t>(256, env_u64("SUIKA_RS_TILE_BYTES", kDefaultTileBytes))) & ~15ull;
-  const int variant = selected_variant();
-  const bool tensor = is_tensor_variant(variant);
-  EncodeTiledFn encode = nullptr;
-  if (tensor) {
-    const int rc = encode_tiled_fn(&encode);
-    if (rc) return rc;
+  int variant = selected_variant();
+  if (variant == kAutoVariant) {
+    bool any_remote = false;
+    for (int64_t i = 0; i < n_desc && !any_remote; ++i) any_remote = !empty_desc(descs[i]) && remote_desc(descs[i]);
+    variant = any_remote ? kAutoRemoteVariant : kAutoLocalVariant;
   }
+  const bool tensor = is_tensor_variant(variant);
+  EncodeTiledFn encode = nullptr;  // looked up at the first tensor entry, after its validation
   std::vector<DevSeg> table;
   std::vector<TensorEntry> tensor_table;
   table.reserve((size_t)n_desc);
@@ -872,6 +882,7 @@ int rs_copy_stage(const rs_copy_desc* descs, int64_t n_desc, void* workspace_dev
       total += d.rows * d.row_bytes;
       if (tensor && tensor_desc(d)) {
         ntiles = sg.tile_begin;  // not a vector-copy entry after all
+        if (!encode && (rc = encode_tiled_fn(&encode))) return rc;
         rc = make_tensor_entries(encode, d, (uint32_t)kTensorShapes[variant - kNumVariants].stage_bytes, ntensor_tiles, tensor_table);
         if (rc) return rc;
         continue;
@@ -1119,7 +1130,7 @@ int noalloc_table_addr(int dev, DevSeg** out) {
 // to the default launch shape.
 int noalloc_variant() {
   const int v = selected_variant();
-  return (!is_tensor_variant(v) && kVariants[v].smem == 0) ? v : 1;
+  return (v != kAutoVariant && !is_tensor_variant(v) && kVariants[v].smem == 0) ? v : 1;
 }
 
 }  // namespace
