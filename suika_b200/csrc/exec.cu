@@ -508,6 +508,12 @@ struct alignas(64) TensorEntry {
   uint32_t box_w;       // box width in 8-byte elements (even: x * 8 stays 16-byte aligned)
   uint32_t box_h;       // box height in rows
   uint32_t box_bytes;   // box_w * 8 * box_h: the bytes a box load always delivers to shared memory
+  // Entries that are column slices of the same source rows (the pieces of a TP grow) form a group
+  // of consecutive entries with one geometry and one tile_begin; the group's boxes are numbered
+  // row band by row band across its members, so CTAs that run at the same time read whole source
+  // rows. Ungrouped entries are groups of one.
+  uint32_t group;       // entries in this entry's group
+  uint32_t member;      // this entry's place in its group
 };
 static_assert(sizeof(TensorEntry) == 320, "TensorEntry layout");
 
@@ -595,15 +601,21 @@ __global__ void __launch_bounds__(32, 1) rs_copy_tensor_kernel(const TensorEntry
   const uint64_t policy = EVICT_FIRST ? l2_evict_first_policy() : 0;
   auto issue = [&]() {
     const uint64_t t = b + issued * g;
-    const TensorEntry& e = cur.locate(ents, nent, t);
+    const TensorEntry& last = cur.locate(ents, nent, t);  // the last member of the group holding box t
+    const int32_t first = cur.si - (int32_t)last.member;
     if (cur.si != acquired) {
-      tensormap_acquire(&e.src);
-      tensormap_acquire(&e.dst);
+      for (int32_t q = first; q <= cur.si; ++q) {
+        tensormap_acquire(&ents[q].src);
+        tensormap_acquire(&ents[q].dst);
+      }
       acquired = cur.si;
     }
-    const uint32_t cb_all = e.col_boxes;
-    const uint32_t lt = (uint32_t)(t - e.tile_begin);
-    const uint32_t rb = lt / cb_all, cb = lt - rb * cb_all;
+    const uint32_t cb_all = last.col_boxes;
+    const uint32_t per_band = last.group * cb_all;
+    const uint32_t lt = (uint32_t)(t - last.tile_begin);
+    const uint32_t rb = lt / per_band, in_band = lt - rb * per_band;
+    const uint32_t m = in_band / cb_all, cb = in_band - m * cb_all;
+    const TensorEntry& e = ents[first + (int32_t)m];
     const uint32_t s = (uint32_t)(issued % STAGES);
     Slot& sl = slots[s];
     sl.dst = &e.dst;
@@ -801,12 +813,17 @@ int encode_2d(EncodeTiledFn fn, CUtensorMap* m, uint64_t addr, uint64_t cols, ui
   return RS_OK;
 }
 
+// Host-side geometry of a TensorEntry (the maps themselves are opaque).
+struct TensorGeom {
+  uint64_t src, src_pitch, rows, row_bytes;
+};
+
 // One rows x row_bytes rectangle -> one TensorEntry, its boxes numbered from `ntiles`. Boxes are
 // 2 KB wide (256 elements; a narrower row gets one box as wide as the row, rounded up to an even
 // element count) so that every box but a row's last starts and ends on 128-byte lines, and as tall
 // as the stage holds.
 int add_tensor_entry(EncodeTiledFn fn, uint64_t src, uint64_t dst, uint64_t rows, uint64_t row_bytes, uint64_t sp, uint64_t dp,
-                     uint32_t stage_bytes, uint64_t& ntiles, std::vector<TensorEntry>& out) {
+                     uint32_t stage_bytes, uint64_t& ntiles, std::vector<TensorEntry>& out, std::vector<TensorGeom>& geom) {
   const uint64_t cols = row_bytes / 8;
   uint64_t bw = std::min<uint64_t>(cols, 256);
   bw += bw & 1;
@@ -819,27 +836,75 @@ int add_tensor_entry(EncodeTiledFn fn, uint64_t src, uint64_t dst, uint64_t rows
   te.box_h = (uint32_t)bh;
   te.box_bytes = (uint32_t)(bw * 8 * bh);
   te.tile_begin = ntiles;
+  te.group = 1;
+  te.member = 0;
   int rc = encode_2d(fn, &te.src, src, cols, rows, sp, (uint32_t)bw, (uint32_t)bh);
   if (!rc) rc = encode_2d(fn, &te.dst, dst, cols, rows, dp, (uint32_t)bw, (uint32_t)bh);
   if (rc) return rc;
   ntiles += (uint64_t)te.col_boxes * ((rows + bh - 1) / bh);
   out.push_back(te);
+  geom.push_back(TensorGeom{src, sp, rows, row_bytes});
   return RS_OK;
 }
 
 // A descriptor -> tensor entries. A contiguous run (one row, or pitches equal to the row) is seen
 // as 2 KB rows plus a shorter last row, so its boxes are full-width.
 int make_tensor_entries(EncodeTiledFn fn, const rs_copy_desc& d, uint32_t stage_bytes, uint64_t& ntiles,
-                        std::vector<TensorEntry>& out) {
+                        std::vector<TensorEntry>& out, std::vector<TensorGeom>& geom) {
   const bool contiguous = d.rows == 1 || (d.src_pitch == d.row_bytes && d.dst_pitch == d.row_bytes);
   const uint64_t total = d.rows * d.row_bytes;
   if (contiguous && total >= 4096) {
     const uint64_t w = 2048, main_rows = total / w, rem = total % w;
-    int rc = add_tensor_entry(fn, d.src_dev, d.dst_dev, main_rows, w, w, w, stage_bytes, ntiles, out);
-    if (!rc && rem) rc = add_tensor_entry(fn, d.src_dev + main_rows * w, d.dst_dev + main_rows * w, 1, rem, rem, rem, stage_bytes, ntiles, out);
+    int rc = add_tensor_entry(fn, d.src_dev, d.dst_dev, main_rows, w, w, w, stage_bytes, ntiles, out, geom);
+    if (!rc && rem)
+      rc = add_tensor_entry(fn, d.src_dev + main_rows * w, d.dst_dev + main_rows * w, 1, rem, rem, rem, stage_bytes, ntiles, out, geom);
     return rc;
   }
-  return add_tensor_entry(fn, d.src_dev, d.dst_dev, d.rows, d.row_bytes, d.src_pitch, d.dst_pitch, stage_bytes, ntiles, out);
+  return add_tensor_entry(fn, d.src_dev, d.dst_dev, d.rows, d.row_bytes, d.src_pitch, d.dst_pitch, stage_bytes, ntiles, out, geom);
+}
+
+// Reorder the tensor entries so that column slices of the same source rows sit together as
+// groups (at most 8: a TP grow by up to 8), and renumber the boxes from `first_tile`. Two entries
+// join when they have the same rows, row length and source pitch, and their sources lie within one
+// source row of each other without overlapping. Returns the total number of boxes.
+uint64_t group_tensor_entries(std::vector<TensorEntry>& ents, const std::vector<TensorGeom>& geom, uint64_t first_tile) {
+  const size_t n = ents.size();
+  std::vector<size_t> idx(n);
+  for (size_t i = 0; i < n; ++i) idx[i] = i;
+  std::sort(idx.begin(), idx.end(), [&](size_t a, size_t b) {
+    const TensorGeom &x = geom[a], &y = geom[b];
+    if (x.src_pitch != y.src_pitch) return x.src_pitch < y.src_pitch;
+    if (x.rows != y.rows) return x.rows < y.rows;
+    if (x.row_bytes != y.row_bytes) return x.row_bytes < y.row_bytes;
+    return x.src < y.src;
+  });
+  std::vector<TensorEntry> out;
+  out.reserve(n);
+  uint64_t tile = first_tile;
+  for (size_t i = 0; i < n;) {
+    const TensorGeom& g0 = geom[idx[i]];
+    size_t j = i + 1;
+    while (j < n && j - i < 8 && g0.rows > 1) {
+      const TensorGeom& gj = geom[idx[j]];
+      const TensorGeom& gp = geom[idx[j - 1]];
+      const bool same = gj.src_pitch == g0.src_pitch && gj.rows == g0.rows && gj.row_bytes == g0.row_bytes;
+      if (!same || gj.src - g0.src >= g0.src_pitch || gj.src - gp.src < gp.row_bytes) break;
+      ++j;
+    }
+    const TensorEntry& lead = ents[idx[i]];
+    const uint64_t boxes = (uint64_t)lead.col_boxes * ((g0.rows + lead.box_h - 1) / lead.box_h);
+    for (size_t q = i; q < j; ++q) {
+      TensorEntry e = ents[idx[q]];
+      e.tile_begin = tile;
+      e.group = (uint32_t)(j - i);
+      e.member = (uint32_t)(q - i);
+      out.push_back(e);
+    }
+    tile += boxes * (j - i);
+    i = j;
+  }
+  ents.swap(out);
+  return tile - first_tile;
 }
 
 }  // namespace
@@ -870,6 +935,7 @@ int rs_copy_stage(const rs_copy_desc* descs, int64_t n_desc, void* workspace_dev
   EncodeTiledFn encode = nullptr;  // looked up at the first tensor entry, after its validation
   std::vector<DevSeg> table;
   std::vector<TensorEntry> tensor_table;
+  std::vector<TensorGeom> tensor_geom;
   table.reserve((size_t)n_desc);
   uint64_t ntiles = 0, total = 0, nremote = 0, ntensor_tiles = 0;
   for (int pass = 0; pass < 2; ++pass) {  // remote entries first, then local ones
@@ -883,7 +949,8 @@ int rs_copy_stage(const rs_copy_desc* descs, int64_t n_desc, void* workspace_dev
       if (tensor && tensor_desc(d)) {
         ntiles = sg.tile_begin;  // not a vector-copy entry after all
         if (!encode && (rc = encode_tiled_fn(&encode))) return rc;
-        rc = make_tensor_entries(encode, d, (uint32_t)kTensorShapes[variant - kNumVariants].stage_bytes, ntensor_tiles, tensor_table);
+        rc = make_tensor_entries(encode, d, (uint32_t)kTensorShapes[variant - kNumVariants].stage_bytes, ntensor_tiles, tensor_table,
+                                 tensor_geom);
         if (rc) return rc;
         continue;
       }
@@ -891,6 +958,7 @@ int rs_copy_stage(const rs_copy_desc* descs, int64_t n_desc, void* workspace_dev
     }
     if (pass == 0) nremote = ntiles;
   }
+  if (!tensor_table.empty()) ntensor_tiles = group_tensor_entries(tensor_table, tensor_geom, 0);
   info->n_entries = (int64_t)table.size();
   info->n_tiles = ntiles;
   info->n_tiles_remote = nremote;

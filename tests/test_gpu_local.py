@@ -205,6 +205,34 @@ def test_tensor_map_kernel_edges(variant, monkeypatch):
     assert torch.equal(dst, want)
 
 
+@pytest.mark.parametrize("variant", ["9", "11", "12", "14"])
+def test_tensor_map_groups_of_column_slices(variant, monkeypatch):
+    """Column slices of the same source rows (the pieces of a TP grow by 2, 3, 4 and 8) are grouped
+    and their boxes interleaved band by band; every target must still get exactly its slice."""
+    monkeypatch.setenv("SUIKA_RS_VARIANT", variant)
+    g = torch.Generator(device=DEV).manual_seed(7)
+    src = torch.randint(0, 255, (64 << 20,), dtype=torch.uint8, device=DEV, generator=g)
+    dst = torch.zeros(64 << 20, dtype=torch.uint8, device=DEV)
+    want = torch.zeros_like(dst)
+    descs, so, do = [], 0, 0
+    for k, rows, rb in ((2, 1000, 11008), (4, 517, 4096), (3, 64, 2064), (8, 77, 1280), (2, 5, 40000)):
+        pitch = k * rb
+        for h in range(k):
+            descs.append((src.data_ptr() + so + h * rb, dst.data_ptr() + do, rows, rb, pitch, rb, 0))
+            want[do:do + rows * rb] = src[so + h * rb: so + h * rb + rows * pitch].view(rows, pitch)[:, :rb].reshape(-1)
+            do = (do + rows * rb + 4095) // 4096 * 4096
+        so = (so + rows * pitch + 4095) // 4096 * 4096
+    assert so <= src.numel() and do <= dst.numel()
+    rng = np.random.default_rng(int(variant))
+    table = np.array([descs[i] for i in rng.permutation(len(descs))], dtype=M.L.COPY_DESC_DTYPE)  # any table order
+    prepared = M.PreparedCopies(table, DEV)
+    info = prepared.launch()
+    assert info.n_entries == 0 and info.n_tensor_entries == len(descs)
+    torch.cuda.synchronize()
+    assert prepared.status() == 0
+    assert torch.equal(dst, want)
+
+
 @pytest.mark.parametrize("variant", ["9", "11", "14"])
 @pytest.mark.parametrize("case", ["cfg2b_mini", "cfg3_mini", "odd_mini", "qwen_grow_mini"])
 def test_reshard_local_tensor_map_shapes_match_reference(case, variant, monkeypatch):
