@@ -717,11 +717,12 @@ uint64_t env_u64(const char* name, uint64_t dflt) {
 
 // Launch shape chosen by SUIKA_RS_VARIANT (1-based): 0-based index below kNumVariants for the
 // vector and bulk-copy kernels, kNumVariants + i for tensor-map shape i. Unset (or 0) selects per
-// table: a table whose entries all stay in this GPU's memory runs the tensor-map shape 11 (4 x 48
-// KB stages, the fastest on a one-GPU relayout); a table with any entry that crosses NVLink runs
-// the vector shape 2, whose CTAs interleave remote and local tiles so both links stay busy.
+// table: a table whose entries all stay in this GPU's memory runs the vector shape 8 (evict-first
+// stores; with its TP-grow slices band-interleaved it is the fastest on a one-GPU relayout); a
+// table with any entry that crosses NVLink runs the vector shape 2, whose CTAs interleave remote
+// and local tiles so both links stay busy.
 constexpr int kAutoVariant = -1;
-constexpr int kAutoLocalVariant = kNumVariants + 2;
+constexpr int kAutoLocalVariant = 7;
 constexpr int kAutoRemoteVariant = 1;
 int selected_variant() {
   const uint64_t v = env_u64("SUIKA_RS_VARIANT", 0);
@@ -791,6 +792,69 @@ int make_entry(const rs_copy_desc& d, int64_t i, uint64_t tile_bytes, uint64_t& 
 
 bool empty_desc(const rs_copy_desc& d) { return d.rows == 0 || d.row_bytes == 0; }
 bool remote_desc(const rs_copy_desc& d) { return (d.flags & RS_COPY_REMOTE) != 0; }
+
+struct IndexedDesc {
+  rs_copy_desc d;
+  int64_t index;  // position in the caller's table, for error messages
+};
+
+// Column slices of the same source rows (the pieces of a TP grow: one source row split between
+// several targets) are read at different times when each slice is its own entry: the first
+// slice's tiles all come before the second's. DRAM then serves each source row twice, half a row
+// at a time, and a one-GPU relayout stays 5 % below a plain copy. Here such slices are cut into
+// row bands of about `band_bytes` per slice and the bands of a group are interleaved (band 0 of
+// every slice, then band 1, ...), so the CTAs that run at the same time read whole source rows.
+// Bands are kept large (8 MB by default, about 64 tiles) because a CTA steps over the entries
+// between its tiles one by one. band_bytes = 0 keeps the table as it is.
+constexpr uint64_t kDefaultBandBytes = 8ull << 20;
+std::vector<IndexedDesc> band_interleave(const std::vector<IndexedDesc>& in, uint64_t band_bytes) {
+  if (band_bytes == 0 || in.size() < 2) return in;
+  const size_t n = in.size();
+  std::vector<size_t> idx;
+  for (size_t i = 0; i < n; ++i)
+    if (in[i].d.rows > 1) idx.push_back(i);
+  std::sort(idx.begin(), idx.end(), [&](size_t a, size_t b) {
+    const rs_copy_desc &x = in[a].d, &y = in[b].d;
+    if (x.src_pitch != y.src_pitch) return x.src_pitch < y.src_pitch;
+    if (x.rows != y.rows) return x.rows < y.rows;
+    if (x.row_bytes != y.row_bytes) return x.row_bytes < y.row_bytes;
+    return x.src_dev < y.src_dev;
+  });
+  std::vector<char> grouped(n, 0);
+  std::vector<IndexedDesc> groups_out;
+  for (size_t i = 0; i < idx.size();) {
+    const rs_copy_desc& d0 = in[idx[i]].d;
+    size_t j = i + 1;
+    while (j < idx.size() && j - i < 8) {
+      const rs_copy_desc& dj = in[idx[j]].d;
+      const rs_copy_desc& dp = in[idx[j - 1]].d;
+      const bool same = dj.src_pitch == d0.src_pitch && dj.rows == d0.rows && dj.row_bytes == d0.row_bytes;
+      if (!same || dj.src_dev - d0.src_dev >= d0.src_pitch || dj.src_dev - dp.src_dev < dp.row_bytes) break;
+      ++j;
+    }
+    const uint64_t band_rows = std::max<uint64_t>(1, band_bytes / d0.row_bytes);
+    if (j - i >= 2 && band_rows < d0.rows) {
+      for (uint64_t r0 = 0; r0 < d0.rows; r0 += band_rows) {
+        const uint64_t nr = std::min(band_rows, d0.rows - r0);
+        for (size_t q = i; q < j; ++q) {
+          IndexedDesc x = in[idx[q]];
+          x.d.src_dev += r0 * x.d.src_pitch;
+          x.d.dst_dev += r0 * x.d.dst_pitch;
+          x.d.rows = nr;
+          groups_out.push_back(x);
+        }
+      }
+      for (size_t q = i; q < j; ++q) grouped[idx[q]] = 1;
+    }
+    i = j;
+  }
+  std::vector<IndexedDesc> out;
+  out.reserve(n + groups_out.size());
+  for (size_t i = 0; i < n; ++i)
+    if (!grouped[i]) out.push_back(in[i]);
+  out.insert(out.end(), groups_out.begin(), groups_out.end());
+  return out;
+}
 
 // An entry the tensor-map kernel takes: this GPU's memory on both sides, 16-byte aligned addresses
 // and pitches (the TMA rules for a tensor's base and strides), whole 8-byte elements per row.
@@ -936,6 +1000,7 @@ int rs_copy_stage(const rs_copy_desc* descs, int64_t n_desc, void* workspace_dev
   std::vector<DevSeg> table;
   std::vector<TensorEntry> tensor_table;
   std::vector<TensorGeom> tensor_geom;
+  std::vector<IndexedDesc> local_vec;  // local entries of the vector copy, placed after the loop
   table.reserve((size_t)n_desc);
   uint64_t ntiles = 0, total = 0, nremote = 0, ntensor_tiles = 0;
   for (int pass = 0; pass < 2; ++pass) {  // remote entries first, then local ones
@@ -954,9 +1019,20 @@ int rs_copy_stage(const rs_copy_desc* descs, int64_t n_desc, void* workspace_dev
         if (rc) return rc;
         continue;
       }
-      table.push_back(sg);
+      if (pass == 0) {
+        table.push_back(sg);
+      } else {
+        ntiles = sg.tile_begin;
+        local_vec.push_back(IndexedDesc{d, i});
+      }
     }
     if (pass == 0) nremote = ntiles;
+  }
+  for (const IndexedDesc& x : band_interleave(local_vec, env_u64("SUIKA_RS_BAND_BYTES", kDefaultBandBytes))) {
+    DevSeg sg;
+    const int rc = make_entry(x.d, x.index, tile_bytes, ntiles, sg, "rs_copy_stage");
+    if (rc) return rc;
+    table.push_back(sg);
   }
   if (!tensor_table.empty()) ntensor_tiles = group_tensor_entries(tensor_table, tensor_geom, 0);
   info->n_entries = (int64_t)table.size();

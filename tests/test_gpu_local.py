@@ -205,11 +205,15 @@ def test_tensor_map_kernel_edges(variant, monkeypatch):
     assert torch.equal(dst, want)
 
 
-@pytest.mark.parametrize("variant", ["9", "11", "12", "14"])
-def test_tensor_map_groups_of_column_slices(variant, monkeypatch):
-    """Column slices of the same source rows (the pieces of a TP grow by 2, 3, 4 and 8) are grouped
-    and their boxes interleaved band by band; every target must still get exactly its slice."""
+@pytest.mark.parametrize("band", ["4096", "65536", "8388608"])
+@pytest.mark.parametrize("variant", ["2", "8", "9", "11", "12", "14"])
+def test_groups_of_column_slices(variant, band, monkeypatch):
+    """Column slices of the same source rows (the pieces of a TP grow by 2, 3, 4 and 8) are grouped:
+    the vector copy cuts them into row bands of SUIKA_RS_BAND_BYTES and interleaves the bands, the
+    tensor-map copy interleaves their boxes band by band. Every target must still get exactly its
+    slice, whatever the table order."""
     monkeypatch.setenv("SUIKA_RS_VARIANT", variant)
+    monkeypatch.setenv("SUIKA_RS_BAND_BYTES", band)
     g = torch.Generator(device=DEV).manual_seed(7)
     src = torch.randint(0, 255, (64 << 20,), dtype=torch.uint8, device=DEV, generator=g)
     dst = torch.zeros(64 << 20, dtype=torch.uint8, device=DEV)
@@ -227,10 +231,37 @@ def test_tensor_map_groups_of_column_slices(variant, monkeypatch):
     table = np.array([descs[i] for i in rng.permutation(len(descs))], dtype=M.L.COPY_DESC_DTYPE)  # any table order
     prepared = M.PreparedCopies(table, DEV)
     info = prepared.launch()
-    assert info.n_entries == 0 and info.n_tensor_entries == len(descs)
+    if int(variant) >= 9:
+        assert info.n_entries == 0 and info.n_tensor_entries == len(descs)
+    else:
+        assert info.n_tensor_entries == 0 and info.n_entries >= len(descs)  # band-split entries
     torch.cuda.synchronize()
     assert prepared.status() == 0
     assert torch.equal(dst, want)
+
+
+@pytest.mark.parametrize("band", ["1024", "65536"])
+@pytest.mark.parametrize("case", ["cfg2b_mini", "grow_dp_tp_mini", "qwen_grow_mini", "cfg3_mini", "odd_mini", "next_step"])
+def test_reshard_local_band_interleaved_matches_reference(case, band, monkeypatch):
+    """The default one-GPU launch (vector copy, TP-grow slices cut into row bands and interleaved),
+    with bands small enough to cut the reduced-width golden cases, equals the reference's digests."""
+    monkeypatch.delenv("SUIKA_RS_VARIANT", raising=False)
+    monkeypatch.setenv("SUIKA_RS_BAND_BYTES", band)
+    g = load_golden(case)
+    cfg = CASES[case]["config"]
+    spl, tpl = cfg.layouts()
+    states = golden_states(cfg, seed=g["seed"])
+    out, info, _ = M.reshard_local(spl, tpl, to_device(states), S.expected_sub_fields(), DEV,
+                                   minimum_est_peers=g["minimum_est_peers"], return_info=True)
+    torch.cuda.synchronize()
+    assert info.n_tensor_entries == 0
+    for rank_s, want in g["ranks"].items():
+        got = out[int(rank_s)]
+        assert list(got) == want["order"]
+        for name, fields in want["digests"].items():
+            for sub, exp in fields.items():
+                t = got[name][sub]
+                assert [list(t.shape), str(t.dtype).replace("torch.", ""), digest(host(t))] == exp, (rank_s, name, sub)
 
 
 @pytest.mark.parametrize("variant", ["9", "11", "14"])
