@@ -704,6 +704,7 @@ constexpr int kNumTensorShapes = sizeof(kTensorShapes) / sizeof(kTensorShapes[0]
 // Workspace layout: the staged vector-copy table, a 256-byte status block (word 0: kStatus* bits),
 // then, for the tensor-map shapes, the TensorEntry table.
 constexpr uint64_t kStatusBytes = 256;
+constexpr uint64_t kBandEntriesPerDesc = 16;  // workspace room per descriptor, in vector-copy entries
 uint64_t status_offset(int64_t n_entries) { return ((uint64_t)n_entries * sizeof(DevSeg) + 255) & ~255ull; }
 uint64_t tensor_offset(int64_t n_entries) { return status_offset(n_entries) + kStatusBytes; }
 
@@ -806,9 +807,12 @@ struct IndexedDesc {
 // every slice, then band 1, ...), so the CTAs that run at the same time read whole source rows.
 // Bands are kept large (8 MB by default, about 64 tiles) because a CTA steps over the entries
 // between its tiles one by one. band_bytes = 0 keeps the table as it is.
+// At most max_out entries come out: a group whose bands would not fit gets fewer, taller bands,
+// or stays whole.
 constexpr uint64_t kDefaultBandBytes = 8ull << 20;
-std::vector<IndexedDesc> band_interleave(const std::vector<IndexedDesc>& in, uint64_t band_bytes) {
-  if (band_bytes == 0 || in.size() < 2) return in;
+std::vector<IndexedDesc> band_interleave(const std::vector<IndexedDesc>& in, uint64_t band_bytes, uint64_t max_out) {
+  if (band_bytes == 0 || in.size() < 2 || max_out <= in.size()) return in;
+  uint64_t budget = max_out - in.size();  // entries the cuts may add
   const size_t n = in.size();
   std::vector<size_t> idx;
   for (size_t i = 0; i < n; ++i)
@@ -832,8 +836,16 @@ std::vector<IndexedDesc> band_interleave(const std::vector<IndexedDesc>& in, uin
       if (!same || dj.src_dev - d0.src_dev >= d0.src_pitch || dj.src_dev - dp.src_dev < dp.row_bytes) break;
       ++j;
     }
-    const uint64_t band_rows = std::max<uint64_t>(1, band_bytes / d0.row_bytes);
-    if (j - i >= 2 && band_rows < d0.rows) {
+    const uint64_t k = j - i;
+    uint64_t band_rows = std::max<uint64_t>(1, band_bytes / d0.row_bytes);
+    uint64_t bands = (d0.rows + band_rows - 1) / band_rows;
+    if (k >= 2 && bands > 1 && k * (bands - 1) > budget) {  // not enough room: fewer, taller bands
+      bands = 1 + budget / k;
+      band_rows = (d0.rows + bands - 1) / bands;
+      bands = (d0.rows + band_rows - 1) / band_rows;
+    }
+    if (k >= 2 && bands > 1) {
+      budget -= k * (bands - 1);
       for (uint64_t r0 = 0; r0 < d0.rows; r0 += band_rows) {
         const uint64_t nr = std::min(band_rows, d0.rows - r0);
         for (size_t q = i; q < j; ++q) {
@@ -977,7 +989,8 @@ extern "C" {
 
 int rs_copy_workspace_bytes(int64_t n_desc, uint64_t* bytes) {
   if (!bytes || n_desc < 0) return efail(RS_ERR_ARG, "rs_copy_workspace_bytes: bad argument");
-  *bytes = (((uint64_t)n_desc * sizeof(DevSeg) + 255) & ~255ull) + kStatusBytes;
+  // room for the row-band cuts of the vector copy (up to kBandEntriesPerDesc entries per descriptor)
+  *bytes = (((uint64_t)n_desc * kBandEntriesPerDesc * sizeof(DevSeg) + 255) & ~255ull) + kStatusBytes;
   const int v = selected_variant();
   if (v == kAutoVariant || is_tensor_variant(v)) *bytes += 2 * (uint64_t)n_desc * sizeof(TensorEntry);  // a run may become 2 entries
   return RS_OK;
@@ -1028,7 +1041,11 @@ int rs_copy_stage(const rs_copy_desc* descs, int64_t n_desc, void* workspace_dev
     }
     if (pass == 0) nremote = ntiles;
   }
-  for (const IndexedDesc& x : band_interleave(local_vec, env_u64("SUIKA_RS_BAND_BYTES", kDefaultBandBytes))) {
+  // entries the caller's workspace holds besides the status block and the tensor maps
+  const uint64_t tensor_room = tensor ? 2 * (uint64_t)n_desc * sizeof(TensorEntry) : 0;
+  const uint64_t room = workspace_bytes > kStatusBytes + tensor_room + 256 ? (workspace_bytes - kStatusBytes - tensor_room - 256) / sizeof(DevSeg) : 0;
+  const uint64_t max_local = std::min<uint64_t>((uint64_t)n_desc * kBandEntriesPerDesc, room > table.size() ? room - table.size() : 0);
+  for (const IndexedDesc& x : band_interleave(local_vec, env_u64("SUIKA_RS_BAND_BYTES", kDefaultBandBytes), max_local)) {
     DevSeg sg;
     const int rc = make_entry(x.d, x.index, tile_bytes, ntiles, sg, "rs_copy_stage");
     if (rc) return rc;
