@@ -234,12 +234,13 @@ def cpu_baseline_block(cfg, n_gpus, threads, budget_s=20.0):
             "sample": smp.describe(reps)}
 
 
-# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per moved byte of the one-GPU pack,
-# from one ncu capture of the same kernel on a 2-layer cfg2b case (1.732 GB moved per launch, above
-# L2): `ncu --set full --clock-control none -k regex:rs_copy -s 3 -c 1 python bench.py --layers 2
-# --steps 3 --warmup 3 --no-e2e --no-cpu-baseline --no-check`. Traffic grows with the moved bytes
-# (every byte is read once and written once), so the full launch's traffic is this ratio x moved.
-DRAM_BYTES_PER_MOVED_BYTE = 1.967
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per moved byte of the one-GPU pack
+# (default launch: evict-first vector copy with row bands), from one ncu capture of the same kernel
+# on a 2-layer cfg2b case (1.732 GB moved per launch, above L2): `ncu --set full --clock-control
+# none -k regex:rs_copy_kernel -s 3 -c 1 python bench.py --layers 2 --steps 3 --warmup 3 --no-e2e
+# --no-cpu-baseline --no-check` gave 1.732 GB read + 1.683 GB written. Traffic grows with the moved
+# bytes (every byte is read once and written once), so the full launch's traffic is this ratio x moved.
+DRAM_BYTES_PER_MOVED_BYTE = 1.972
 
 
 def rank_bytes_ops(ops) -> dict:
