@@ -284,9 +284,9 @@ int rs_copy_workspace_bytes(int64_t n_desc, uint64_t* bytes);
  * cudaStream_t; NULL = legacy default stream). Fills *info for rs_copy_run. The launch shape is
  * SUIKA_RS_VARIANT's; unset, a table with no RS_COPY_REMOTE entry takes the vector shape 8 and
  * any other table the vector shape 2. For the vector shapes, local entries that are column slices
- * of the same source rows (a TP grow's pieces) are grouped, and the group's tiles are numbered by
- * row bands of about SUIKA_RS_BAND_BYTES (default 8 MB) per slice, so that whole source rows are
- * read at once. */
+ * of the same source rows (a TP grow's pieces) are cut into row bands of about
+ * SUIKA_RS_BAND_BYTES (default 8 MB) per slice and interleaved, so that whole source rows are read
+ * at once; rs_launch_info.n_entries counts the entries after that cut. */
 int rs_copy_stage(const rs_copy_desc* descs, int64_t n_desc, void* workspace_dev, uint64_t workspace_bytes,
                   void* stream, rs_launch_info* info);
 /* Launch the copy kernel over a staged table (asynchronous; may be repeated while the workspace

@@ -36,34 +36,20 @@ int cuda_fail(cudaError_t e, const char* what) {
 }
 
 // One table entry as the kernel reads it (72 bytes).
-//
-// Column slices of the same source rows (a TP grow's pieces: every source row split between
-// several targets) form a group of consecutive entries with one geometry and one tile_begin. The
-// group's tiles are numbered row band by row band across its members (band 0 of every member, then
-// band 1, ...), so the CTAs that run at the same time read whole source rows; an ungrouped entry is
-// a group of one.
 struct DevSeg {
   uint64_t src;
   uint64_t dst;
   uint64_t src_pitch;
   uint64_t dst_pitch;
-  uint64_t tile_begin;   // global index of this entry's first tile (its group's first tile)
+  uint64_t tile_begin;   // global index of this entry's first tile
   uint64_t row_bytes;
-  uint32_t col_bytes;    // bytes of one column chunk when rows are split, else row_bytes (at most 1 GB)
-  uint32_t band_tiles;   // grouped entry: tiles of one member per row band (whole row groups)
+  uint64_t col_bytes;    // bytes of one column chunk when rows are split, else row_bytes
   uint32_t rows;
   uint32_t rows_per_tile;
   uint32_t col_tiles;    // column chunks per row (1 when whole rows fit in a tile)
-  uint32_t shape;        // bits 0-7: log2 of the vector width (0..4); 8-15: members of the group; 16-23: this member
+  uint32_t vshift;       // log2 of the vector width (0..4)
 };
 static_assert(sizeof(DevSeg) == 72, "DevSeg layout");
-
-__host__ __device__ __forceinline__ uint32_t seg_vshift(const DevSeg& s) { return s.shape & 0xffu; }
-__host__ __device__ __forceinline__ uint32_t seg_group(const DevSeg& s) { return (s.shape >> 8) & 0xffu; }
-__host__ __device__ __forceinline__ uint32_t seg_member(const DevSeg& s) { return (s.shape >> 16) & 0xffu; }
-__host__ __device__ __forceinline__ uint32_t seg_shape(uint32_t vshift, uint32_t group, uint32_t member) {
-  return vshift | (group << 8) | (member << 16);
-}
 
 constexpr uint64_t kDefaultTileBytes = 128 * 1024;
 
@@ -250,46 +236,21 @@ struct Tile {
   uint32_t nr, vshift;
 };
 
-// Tile lt (counted from 0 within the entry) of entry s.
-__device__ __forceinline__ Tile tile_of(const DevSeg& s, uint64_t lt) {
+__device__ __forceinline__ Tile tile_of(const DevSeg& s, uint64_t t) {
   Tile x;
+  const uint64_t lt = t - s.tile_begin;
   const uint64_t rg = lt / s.col_tiles;
   const uint64_t col = lt - rg * s.col_tiles;
   const uint64_t r0 = rg * s.rows_per_tile;
   x.nr = (uint32_t)min((uint64_t)s.rows_per_tile, (uint64_t)s.rows - r0);
   const uint64_t c0 = col * s.col_bytes;
-  x.nb = min((uint64_t)s.col_bytes, s.row_bytes - c0);
+  x.nb = min(s.col_bytes, s.row_bytes - c0);
   x.sp = s.src_pitch;
   x.dp = s.dst_pitch;
   x.src = reinterpret_cast<const char*>(s.src) + r0 * x.sp + c0;
   x.dst = reinterpret_cast<char*>(s.dst) + r0 * x.dp + c0;
-  x.vshift = seg_vshift(s);
+  x.vshift = s.vshift;
   return x;
-}
-
-// Global tile t, found in the group whose last member is segs[si]: which member, and which of its
-// tiles. The host keeps a group's tile count below 2^31, so the arithmetic is 32-bit.
-__device__ __forceinline__ Tile tile_in_group(const DevSeg* __restrict__ segs, int32_t si, const DevSeg& last, uint64_t t) {
-  const uint32_t k = seg_group(last);
-  if (k <= 1) return tile_of(last, t - last.tile_begin);
-  const uint32_t lt = (uint32_t)(t - last.tile_begin);
-  const uint32_t per = (last.rows + last.rows_per_tile - 1) / last.rows_per_tile * last.col_tiles;  // tiles of each member
-  const uint32_t bt = last.band_tiles;
-  const uint32_t full = per / bt;  // full bands
-  const uint32_t span = k * bt;
-  uint32_t band = lt / span, m, within;
-  if (band < full) {
-    const uint32_t rem = lt - band * span;
-    m = rem / bt;
-    within = rem - m * bt;
-  } else {  // the last, shorter band
-    const uint32_t tail = per - full * bt;
-    const uint32_t rem = lt - full * span;
-    m = rem / tail;
-    within = rem - m * tail;
-    band = full;
-  }
-  return tile_of(segs[si - (int32_t)seg_member(last) + (int32_t)m], (uint64_t)band * bt + within);
 }
 
 struct Schedule {
@@ -308,8 +269,7 @@ struct Schedule {
     if (!hr && !hl) return false;
     const bool take_r = hr && (!hl || d_r * n_l <= d_l * n_r);
     TileCursor& c = take_r ? rc : lc;
-    const DevSeg& last = c.locate(segs, nseg);
-    out = tile_in_group(segs, c.si, last, c.t);
+    out = tile_of(c.locate(segs, nseg), c.t);
     c.t += gridDim.x;
     if (take_r) ++d_r; else ++d_l;
     return true;
@@ -744,6 +704,7 @@ constexpr int kNumTensorShapes = sizeof(kTensorShapes) / sizeof(kTensorShapes[0]
 // Workspace layout: the staged vector-copy table, a 256-byte status block (word 0: kStatus* bits),
 // then, for the tensor-map shapes, the TensorEntry table.
 constexpr uint64_t kStatusBytes = 256;
+constexpr uint64_t kBandEntriesPerDesc = 16;  // workspace room per descriptor, in vector-copy entries
 uint64_t status_offset(int64_t n_entries) { return ((uint64_t)n_entries * sizeof(DevSeg) + 255) & ~255ull; }
 uint64_t tensor_offset(int64_t n_entries) { return status_offset(n_entries) + kStatusBytes; }
 
@@ -811,16 +772,15 @@ int make_entry(const rs_copy_desc& d, int64_t i, uint64_t tile_bytes, uint64_t& 
   s.dst_pitch = d.dst_pitch;
   s.rows = (uint32_t)d.rows;
   s.row_bytes = d.row_bytes;
-  s.shape = seg_shape(vector_shift(d), 1, 0);
-  s.band_tiles = 0;
+  s.vshift = vector_shift(d);
   s.tile_begin = ntiles;
   if (d.row_bytes >= tile_bytes) {
-    s.col_bytes = (uint32_t)tile_bytes;
+    s.col_bytes = tile_bytes;
     s.col_tiles = (uint32_t)((d.row_bytes + tile_bytes - 1) / tile_bytes);
     s.rows_per_tile = 1;
     ntiles += (uint64_t)s.col_tiles * d.rows;
   } else {
-    s.col_bytes = (uint32_t)d.row_bytes;
+    s.col_bytes = d.row_bytes;
     s.col_tiles = 1;
     // Whole rows per tile, capped so that every in-tile offset fits 32 bits.
     const uint64_t pitch = std::max(d.src_pitch, d.dst_pitch);
@@ -834,81 +794,78 @@ int make_entry(const rs_copy_desc& d, int64_t i, uint64_t tile_bytes, uint64_t& 
 bool empty_desc(const rs_copy_desc& d) { return d.rows == 0 || d.row_bytes == 0; }
 bool remote_desc(const rs_copy_desc& d) { return (d.flags & RS_COPY_REMOTE) != 0; }
 
-// Column slices of the same source rows (the pieces of a TP grow: one source row split between
-// several targets) are read at different times when each slice's tiles follow the previous
-// slice's: DRAM then serves each source row twice, half a row at a time, and a one-GPU relayout
-// stays 5 % below a plain copy. Such slices become one group (DevSeg above) whose tiles are
-// numbered by row bands of about `band_bytes` per member, so the CTAs that run at the same time
-// read whole source rows. Members need one geometry (rows, row length, source pitch, tiling); their
-// sources lie within one source row of each other without overlapping. At most 8 per group.
-constexpr uint64_t kDefaultBandBytes = 8ull << 20;
+struct IndexedDesc {
+  rs_copy_desc d;
+  int64_t index;  // position in the caller's table, for error messages
+};
 
-// Number the local entries' tiles from `first_tile`, grouping column slices; ungrouped entries keep
-// their order and come first. Returns the next free tile index.
-uint64_t group_local_entries(std::vector<DevSeg>& ents, uint64_t band_bytes, uint64_t first_tile) {
-  const size_t n = ents.size();
-  auto tiles_of = [](const DevSeg& e) -> uint64_t {
-    return (uint64_t)((e.rows + e.rows_per_tile - 1) / e.rows_per_tile) * e.col_tiles;
-  };
+// Column slices of the same source rows (the pieces of a TP grow: one source row split between
+// several targets) are read at different times when each slice is its own entry: the first
+// slice's tiles all come before the second's. DRAM then serves each source row twice, half a row
+// at a time, and a one-GPU relayout stays 5 % below a plain copy. Here such slices are cut into
+// row bands of about `band_bytes` per slice and the bands of a group are interleaved (band 0 of
+// every slice, then band 1, ...), so the CTAs that run at the same time read whole source rows.
+// Bands are kept large (8 MB by default, about 64 tiles) because a CTA steps over the entries
+// between its tiles one by one. band_bytes = 0 keeps the table as it is.
+// At most max_out entries come out: a group whose bands would not fit gets fewer, taller bands,
+// or stays whole.
+constexpr uint64_t kDefaultBandBytes = 8ull << 20;
+std::vector<IndexedDesc> band_interleave(const std::vector<IndexedDesc>& in, uint64_t band_bytes, uint64_t max_out) {
+  if (band_bytes == 0 || in.size() < 2 || max_out <= in.size()) return in;
+  uint64_t budget = max_out - in.size();  // entries the cuts may add
+  const size_t n = in.size();
   std::vector<size_t> idx;
   for (size_t i = 0; i < n; ++i)
-    if (ents[i].rows > 1) idx.push_back(i);
+    if (in[i].d.rows > 1) idx.push_back(i);
   std::sort(idx.begin(), idx.end(), [&](size_t a, size_t b) {
-    const DevSeg &x = ents[a], &y = ents[b];
+    const rs_copy_desc &x = in[a].d, &y = in[b].d;
     if (x.src_pitch != y.src_pitch) return x.src_pitch < y.src_pitch;
     if (x.rows != y.rows) return x.rows < y.rows;
     if (x.row_bytes != y.row_bytes) return x.row_bytes < y.row_bytes;
-    if (x.rows_per_tile != y.rows_per_tile) return x.rows_per_tile < y.rows_per_tile;
-    return x.src < y.src;
+    return x.src_dev < y.src_dev;
   });
   std::vector<char> grouped(n, 0);
-  std::vector<std::vector<size_t>> groups;
-  std::vector<uint32_t> group_band;
+  std::vector<IndexedDesc> groups_out;
   for (size_t i = 0; i < idx.size();) {
-    const DevSeg& e0 = ents[idx[i]];
+    const rs_copy_desc& d0 = in[idx[i]].d;
     size_t j = i + 1;
     while (j < idx.size() && j - i < 8) {
-      const DevSeg& ej = ents[idx[j]];
-      const DevSeg& ep = ents[idx[j - 1]];
-      const bool same = ej.src_pitch == e0.src_pitch && ej.rows == e0.rows && ej.row_bytes == e0.row_bytes &&
-                        ej.rows_per_tile == e0.rows_per_tile && ej.col_tiles == e0.col_tiles;
-      if (!same || ej.src - e0.src >= e0.src_pitch || ej.src - ep.src < ep.row_bytes) break;
+      const rs_copy_desc& dj = in[idx[j]].d;
+      const rs_copy_desc& dp = in[idx[j - 1]].d;
+      const bool same = dj.src_pitch == d0.src_pitch && dj.rows == d0.rows && dj.row_bytes == d0.row_bytes;
+      if (!same || dj.src_dev - d0.src_dev >= d0.src_pitch || dj.src_dev - dp.src_dev < dp.row_bytes) break;
       ++j;
     }
-    const uint64_t k = j - i, per = tiles_of(e0);
-    const uint64_t row_group_bytes = (uint64_t)e0.rows_per_tile * e0.row_bytes;  // rows_per_tile is 1 when rows are split
-    const uint64_t band_rg = std::max<uint64_t>(1, band_bytes / std::max<uint64_t>(1, row_group_bytes));
-    const uint64_t bt = band_rg * e0.col_tiles;
-    if (k >= 2 && bt < per && k * per < (1ull << 31)) {
-      groups.emplace_back(idx.begin() + i, idx.begin() + j);
-      group_band.push_back((uint32_t)bt);
+    const uint64_t k = j - i;
+    uint64_t band_rows = std::max<uint64_t>(1, band_bytes / d0.row_bytes);
+    uint64_t bands = (d0.rows + band_rows - 1) / band_rows;
+    if (k >= 2 && bands > 1 && k * (bands - 1) > budget) {  // not enough room: fewer, taller bands
+      bands = 1 + budget / k;
+      band_rows = (d0.rows + bands - 1) / bands;
+      bands = (d0.rows + band_rows - 1) / band_rows;
+    }
+    if (k >= 2 && bands > 1) {
+      budget -= k * (bands - 1);
+      for (uint64_t r0 = 0; r0 < d0.rows; r0 += band_rows) {
+        const uint64_t nr = std::min(band_rows, d0.rows - r0);
+        for (size_t q = i; q < j; ++q) {
+          IndexedDesc x = in[idx[q]];
+          x.d.src_dev += r0 * x.d.src_pitch;
+          x.d.dst_dev += r0 * x.d.dst_pitch;
+          x.d.rows = nr;
+          groups_out.push_back(x);
+        }
+      }
       for (size_t q = i; q < j; ++q) grouped[idx[q]] = 1;
     }
     i = j;
   }
-  std::vector<DevSeg> out;
-  out.reserve(n);
-  uint64_t tile = first_tile;
-  for (size_t i = 0; i < n; ++i) {
-    if (grouped[i]) continue;
-    DevSeg e = ents[i];
-    e.tile_begin = tile;
-    tile += tiles_of(e);
-    out.push_back(e);
-  }
-  for (size_t g = 0; g < groups.size(); ++g) {
-    const std::vector<size_t>& mem = groups[g];
-    for (size_t q = 0; q < mem.size(); ++q) {
-      DevSeg e = ents[mem[q]];
-      e.tile_begin = tile;
-      e.band_tiles = group_band[g];
-      e.shape = seg_shape(seg_vshift(e), (uint32_t)mem.size(), (uint32_t)q);
-      out.push_back(e);
-    }
-    tile += tiles_of(ents[mem[0]]) * mem.size();
-  }
-  ents.swap(out);
-  return tile;
+  std::vector<IndexedDesc> out;
+  out.reserve(n + groups_out.size());
+  for (size_t i = 0; i < n; ++i)
+    if (!grouped[i]) out.push_back(in[i]);
+  out.insert(out.end(), groups_out.begin(), groups_out.end());
+  return out;
 }
 
 // An entry the tensor-map kernel takes: this GPU's memory on both sides, 16-byte aligned addresses
@@ -1032,7 +989,8 @@ extern "C" {
 
 int rs_copy_workspace_bytes(int64_t n_desc, uint64_t* bytes) {
   if (!bytes || n_desc < 0) return efail(RS_ERR_ARG, "rs_copy_workspace_bytes: bad argument");
-  *bytes = (((uint64_t)n_desc * sizeof(DevSeg) + 255) & ~255ull) + kStatusBytes;
+  // room for the row-band cuts of the vector copy (up to kBandEntriesPerDesc entries per descriptor)
+  *bytes = (((uint64_t)n_desc * kBandEntriesPerDesc * sizeof(DevSeg) + 255) & ~255ull) + kStatusBytes;
   const int v = selected_variant();
   if (v == kAutoVariant || is_tensor_variant(v)) *bytes += 2 * (uint64_t)n_desc * sizeof(TensorEntry);  // a run may become 2 entries
   return RS_OK;
@@ -1055,7 +1013,7 @@ int rs_copy_stage(const rs_copy_desc* descs, int64_t n_desc, void* workspace_dev
   std::vector<DevSeg> table;
   std::vector<TensorEntry> tensor_table;
   std::vector<TensorGeom> tensor_geom;
-  std::vector<DevSeg> local_vec;  // local entries of the vector copy, numbered after the loop
+  std::vector<IndexedDesc> local_vec;  // local entries of the vector copy, placed after the loop
   table.reserve((size_t)n_desc);
   uint64_t ntiles = 0, total = 0, nremote = 0, ntensor_tiles = 0;
   for (int pass = 0; pass < 2; ++pass) {  // remote entries first, then local ones
@@ -1078,13 +1036,21 @@ int rs_copy_stage(const rs_copy_desc* descs, int64_t n_desc, void* workspace_dev
         table.push_back(sg);
       } else {
         ntiles = sg.tile_begin;
-        local_vec.push_back(sg);
+        local_vec.push_back(IndexedDesc{d, i});
       }
     }
     if (pass == 0) nremote = ntiles;
   }
-  ntiles = group_local_entries(local_vec, env_u64("SUIKA_RS_BAND_BYTES", kDefaultBandBytes), ntiles);
-  table.insert(table.end(), local_vec.begin(), local_vec.end());
+  // entries the caller's workspace holds besides the status block and the tensor maps
+  const uint64_t tensor_room = tensor ? 2 * (uint64_t)n_desc * sizeof(TensorEntry) : 0;
+  const uint64_t room = workspace_bytes > kStatusBytes + tensor_room + 256 ? (workspace_bytes - kStatusBytes - tensor_room - 256) / sizeof(DevSeg) : 0;
+  const uint64_t max_local = std::min<uint64_t>((uint64_t)n_desc * kBandEntriesPerDesc, room > table.size() ? room - table.size() : 0);
+  for (const IndexedDesc& x : band_interleave(local_vec, env_u64("SUIKA_RS_BAND_BYTES", kDefaultBandBytes), max_local)) {
+    DevSeg sg;
+    const int rc = make_entry(x.d, x.index, tile_bytes, ntiles, sg, "rs_copy_stage");
+    if (rc) return rc;
+    table.push_back(sg);
+  }
   if (!tensor_table.empty()) ntensor_tiles = group_tensor_entries(tensor_table, tensor_geom, 0);
   info->n_entries = (int64_t)table.size();
   info->n_tiles = ntiles;
