@@ -732,6 +732,9 @@ def main():
                     help="N > 1, push: DP-replica fan-out (suika_b200.fanout); the default workloads have no replicas")
     ap.add_argument("--direction", choices=["pull", "push"], default="push",
                     help="N > 1: target ranks read their pieces (pull) or source ranks write them (push)")
+    ap.add_argument("--checkpoint", action="store_true",
+                    help="time checkpoint resume instead: one target rank's state built on the GPU from host shards "
+                         "(1 GPU; ours against the reference's CPU execute plus a copy to the GPU)")
     ap.add_argument("--peer-probe", action="store_true",
                     help="time the copy kernel's peer patterns between GPU 0 and GPU 1 instead (one process, 2 GPUs)")
     ap.add_argument("--peer-gib", type=float, default=2.0)
@@ -741,6 +744,9 @@ def main():
     args = ap.parse_args()
     if args.peer_probe:
         run_peer_probe(args)
+        return
+    if args.checkpoint:
+        print(json.dumps(run_checkpoint(args)), flush=True)
         return
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
@@ -796,6 +802,76 @@ def main():
     if res is not None:
         print(json.dumps(res), flush=True)
 
+
+
+# ---------------------------------------------------------------------------------------------
+# --checkpoint: checkpoint resume, one target rank built from host-resident source shards (1 GPU)
+# ---------------------------------------------------------------------------------------------
+def run_checkpoint(args):
+    """Checkpoint resume (Suika/migration.py:1156-1305): every source shard a target rank needs is
+    in host memory (loaded from disk; loading is not timed), and the rank's new state must end up on
+    its GPU. Workload: target rank 0 of the cfg3 family (Llama2-13B-shaped, TP8 -> TP4 x PP2) on a
+    layer sample. A step:
+      ours: execute_param_transfer(..., fake_source_state_dicts=...) -- the needed shards are
+        gathered into one page-locked arena and one launch writes every target on the GPU, reading
+        host memory over PCIe;
+      reference: its execute_param_transfer on device "cpu" (migration.py:1235-1244; restated in
+        oracle/nccl_port.checkpoint_rank, pinned to the golden digests), then every target copied
+        to the GPU.
+    Wall time per step after a synchronize on both sides; the two results are compared byte for
+    byte once, outside the timing."""
+    from oracle import nccl_port as P
+    from oracle import restate as O
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cfg = workload(8, args.layers or 8)
+    spl, tpl = cfg.layouts()
+    rank = 0
+    mep = 1 if M.is_ib_enabled() else 2
+    ops = O.schedule(spl, tpl, minimum_est_peers=mep)
+    src_ranks = sorted({o.src for o in ops if o.dst == rank})
+    states = S.host_states(spl, S.SUBFIELDS, seed=0, ranks=src_ranks)
+    fake = {r: {n: {s: S.to_torch(a, k) for (s, k), a in zip(S.SUBFIELDS, e.values())} for n, e in st.items()}
+            for r, st in states.items()}
+    del states
+    exp = S.expected_sub_fields()
+    subfields = [(s, k == "meta", S.TORCH_DTYPE[k]) for s, k in S.SUBFIELDS]
+    sched = M.schedule_param_transfer(spl, tpl)
+    target_bytes = sum(o.numel for o in ops if o.dst == rank) * STATE_BYTES_PER_ELEM
+
+    def ours():
+        return M.execute_param_transfer(sched, fake.get(rank, {}), dev, exp, fake_source_state_dicts=fake, rank=rank)
+
+    def reference():
+        out = P.checkpoint_rank(ops, fake, subfields, rank)
+        return {n: {s: t.to(dev) for s, t in e.items()} for n, e in out.items()}
+
+    res = {}
+    for name, fn in (("ours", ours), ("reference", reference)):
+        times = []
+        for i in range(args.warmup + args.steps):
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            out = fn()
+            torch.cuda.synchronize()
+            if i >= args.warmup:
+                times.append(time.perf_counter() - t0)
+            if i < args.warmup + args.steps - 1:
+                del out
+        res[name] = (statistics.median(times), out)
+    a, b = res["ours"][1], res["reference"][1]
+    same = list(a) == list(b) and all(torch.equal(a[n][s].reshape(-1), b[n][s].reshape(-1)) for n in a for s in a[n])
+    t_ours, t_ref = res["ours"][0], res["reference"][0]
+    return {"metric": "checkpoint resume: one target rank's training state built on its GPU from host shards",
+            "value": round(target_bytes / t_ours / 1e9, 3), "unit": "GB/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(t_ours * 1e3, 2), "higher_is_better": True,
+            "config": {"workload": f"target rank {rank} of {cfg.note} ({cfg.spec.n_layers} layers), full training state, "
+                                   f"source shards of ranks {src_ranks} in host memory"},
+            "target_gb": round(target_bytes / 1e9, 3), "reference_ms_per_step": round(t_ref * 1e3, 2),
+            "reference_gbs": round(target_bytes / t_ref / 1e9, 3), "speedup": round(t_ref / t_ours, 2),
+            "check": {"byte_equal": bool(same)},
+            "reference_path": "oracle/nccl_port.checkpoint_rank (execute on device cpu, Suika/migration.py:1235-1244) + .to(cuda)",
+            "host_threads": torch.get_num_threads()}
 
 
 # ---------------------------------------------------------------------------------------------

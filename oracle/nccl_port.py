@@ -104,3 +104,45 @@ def execute_rank(ops: Sequence[Op], source_state_dict: Dict[str, Dict[str, torch
     if cuda_gc:
         _cuda_gc()
     return out
+
+
+def checkpoint_rank(ops: Sequence[Op], fake_source_state_dicts: Dict[int, Dict[str, Dict[str, torch.Tensor]]],
+                    subfields: Sequence[Tuple[str, bool, torch.dtype]], rank: int) -> Dict[str, Dict[str, torch.Tensor]]:
+    """One rank's checkpoint resume as the reference runs it: execute_param_transfer with
+    fake_source_state_dicts on device "cpu" (Suika/migration.py:1235-1244). A piece from another
+    rank is get_send_tensor of that rank's host shard (the fake-source branch, :475-482); a piece of
+    the rank's own source goes through the deferred self branch (:448-459), so it lands after the
+    others; each target is torch.cat of its pieces along the slice dim, or a clone (:531-545). A
+    piece this rank would send to another is still cut out (get_send_tensor, :442-446) and then not
+    sent (:461-463), as the reference does."""
+    own = fake_source_state_dicts.get(rank, {})
+    deferred = []
+    target: Dict[str, Dict[str, list]] = {}
+    slice_dim: Dict[str, int] = {}
+    for op in ops:
+        if op.dst != rank and op.src != rank:
+            continue
+        if op.dst == rank and op.name not in target:
+            target[op.name] = {s: [] for s, _m, _d in subfields}
+            slice_dim[op.name] = None if op.dst_tp is None else op.dst_tp[0]
+        if op.src == rank:
+            if op.name not in own:
+                raise AssertionError(f"[{rank}]: param missing in source {op.name}")
+            for s, meta, _dt in subfields:
+                t = own[op.name][s]
+                piece = t if meta else send_piece(t, op.src_tp, op.dst_tp)
+                if op.dst == rank:
+                    deferred.append((op.name, s, piece))
+        else:
+            src = fake_source_state_dicts[op.src][op.name]
+            for s, meta, _dt in subfields:
+                target[op.name][s].append(src[s] if meta else send_piece(src[s], op.src_tp, op.dst_tp))
+    for name, s, t in deferred:
+        target[name][s].append(t)
+    out: Dict[str, Dict[str, torch.Tensor]] = {}
+    for name, fields in target.items():
+        out[name] = {}
+        for s, meta, _dt in subfields:
+            pieces = fields[s]
+            out[name][s] = torch.cat(pieces, dim=slice_dim[name]) if (not meta and len(pieces) > 1) else pieces[0].clone()
+    return out

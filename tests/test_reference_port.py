@@ -71,3 +71,30 @@ def test_nccl_port_matches_reference_digests(case):
                 if sub == "step":  # compared by value elsewhere; the port's dtype follows the sub-field
                     continue
                 assert (gs, gd, gh) == (shape, dtype, sha), (rank_s, name, sub)
+
+
+@pytest.mark.parametrize("case", ["cfg3_mini", "odd_mini", "hetero_mini", "grow_dp_tp_mini", "next_step"])
+def test_checkpoint_port_matches_reference_digests(case):
+    """The port of the reference's checkpoint resume (execute on the CPU from every rank's host
+    shard), which bench.py --checkpoint times as the reference's path, rebuilds the golden targets."""
+    from oracle import nccl_port as P
+    from oracle import restate as O
+    from suika_b200 import synthetic as S
+    from tests.helpers import SUBS, digest
+    g = load_golden(case)
+    cfg = CASES[case]["config"]
+    spl, tpl = cfg.layouts()
+    states = S.host_states(spl, SUBS, seed=g["seed"], distinct_steps=True)
+    fake = {r: {n: {s: S.to_torch(a, k) for (s, k), a in zip(SUBS, e.values())} for n, e in st.items()} for r, st in states.items()}
+    subfields = [(s, k == "meta", S.TORCH_DTYPE[k]) for s, k in SUBS]
+    ops = O.schedule(spl, tpl, minimum_est_peers=g["minimum_est_peers"])
+    for rank_s, want in g["ranks"].items():
+        out = P.checkpoint_rank(ops, fake, subfields, int(rank_s))
+        assert list(out) == want["order"]
+        for name, fields in want["digests"].items():
+            for sub, (shape, dtype, sha) in fields.items():
+                t = out[name][sub]
+                h = t.view(torch.uint16) if t.dtype == torch.bfloat16 else t
+                if sub == "step":
+                    continue
+                assert [list(t.shape), str(t.dtype).replace("torch.", ""), digest(h.numpy())] == [shape, dtype, sha], (rank_s, name, sub)
