@@ -1283,6 +1283,9 @@ def execute_param_transfer(transfer_ops: TransferSchedule, source_state_dict, de
     return target
 
 
+_HOST_CHUNK_BYTES = 256 << 20  # checkpoint resume: bytes of source shards gathered per launch
+
+
 def execute_from_host(plan: Plan, rank: int, source_state_dict, fake_source_state_dicts, expected_sub_fields,
                       device: torch.device) -> Dict[str, Dict[str, torch.Tensor]]:
     """Checkpoint resume on B200: this rank's targets from host-resident source shards.
@@ -1309,7 +1312,7 @@ def execute_from_host(plan: Plan, rank: int, source_state_dict, fake_source_stat
             raise RuntimeError(f"checkpoint source {name}[{sub}] of rank {sr} is not in host memory")
         return t.contiguous()
 
-    # 1. the needed source slots, gathered into one page-locked arena the GPU can read directly
+    # 1. the needed source slots go into one page-locked arena the GPU reads directly
     hs = [host_src(int(ss["src_rank"]), plan.names[int(ss["name_id"])], subs[int(ss["subfield"])]) for ss in prog.src_slots]
     nb = np.array([t.numel() * t.element_size() for t in hs], np.uint64)
     off = np.zeros(len(hs), np.uint64)
@@ -1317,11 +1320,9 @@ def execute_from_host(plan: Plan, rank: int, source_state_dict, fake_source_stat
         off[1:] = np.cumsum((nb[:-1] + np.uint64(255)) // np.uint64(256) * np.uint64(256))
     total = int(off[-1] + nb[-1]) if len(hs) else 0
     arena = torch.empty(max(total, 1), dtype=torch.uint8, pin_memory=True)
-    for t, o, n in zip(hs, off, nb):
-        arena[int(o):int(o) + int(n)].copy_(t.reshape(-1).view(torch.uint8))
     dp = C.c_void_p()
     L.check(L.load().rs_host_device_pointer(C.c_void_p(arena.data_ptr()), C.byref(dp)))
-    # 2. targets on the device, filled by one launch reading host memory over PCIe
+    # 2. targets on the device; their copy table, reading host memory over PCIe
     dst_t = []
     for ds in prog.dst_slots:
         shape = tuple(int(x) for x in ds["shape"][: ds["ndim"]])
@@ -1329,6 +1330,27 @@ def execute_from_host(plan: Plan, rank: int, source_state_dict, fake_source_stat
     table = prog.resolve(off + np.uint64(dp.value), nb, np.array([x.data_ptr() for x in dst_t], np.uint64),
                          np.array([x.numel() * x.element_size() for x in dst_t], np.uint64))
     table["flags"] = L.RS_COPY_REMOTE
+    # 3. gather and copy in chunks of source slots: while the GPU reads chunk k over PCIe, the host
+    #    gathers chunk k + 1 into the arena, so the two overlap
+    chunk_of = np.zeros(len(hs), np.int64)
+    acc, c = 0, 0
+    for i in range(len(hs)):
+        if acc >= _HOST_CHUNK_BYTES:
+            c, acc = c + 1, 0
+        chunk_of[i] = c
+        acc += int(nb[i])
+    seg_chunk = chunk_of[prog.segments["src_slot"]] if len(prog.segments) else np.zeros(0, np.int64)
+    n_chunks = int(chunk_of.max()) + 1 if len(hs) else 0
+    # every chunk's table is staged before the gather starts, so a chunk's launch is a kernel launch only
+    chunks = [PreparedCopies(table[seg_chunk == k], device) if np.any(seg_chunk == k) else None for k in range(n_chunks)]
+    launched = []
+    for k in range(n_chunks):
+        for i in np.nonzero(chunk_of == k)[0]:
+            o, n = int(off[i]), int(nb[i])
+            arena[o:o + n].copy_(hs[i].reshape(-1).view(torch.uint8))
+        if chunks[k] is not None:
+            chunks[k].launch()
+            launched.append(chunks[k])
     ent: Dict[str, Dict[str, torch.Tensor]] = {}
     for ds, x in zip(prog.dst_slots, dst_t):
         ent.setdefault(plan.names[ds["name_id"]], {})[subs[ds["subfield"]]] = x
@@ -1340,9 +1362,12 @@ def execute_from_host(plan: Plan, rank: int, source_state_dict, fake_source_stat
         meta.add(v, x)
         ent.setdefault(name, {})[s] = x
     md, stage = meta.descs()
-    prepared = PreparedCopies(np.concatenate([table, md]), device)
-    prepared.launch()
-    prepared.check()  # synchronises: the arena and the staging buffer may go after this
+    if len(md):
+        p = PreparedCopies(md, device)
+        p.launch()
+        launched.append(p)
+    for p in launched:
+        p.check()  # synchronises: the arena and the staging buffer may go after this
     del arena, stage
     return {plan.names[n]: {s: ent[plan.names[n]][s] for s in subs if s in ent[plan.names[n]]} for n in _name_order(plan, rank)}
 
