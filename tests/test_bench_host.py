@@ -82,3 +82,40 @@ def test_reference_activation_sequence_matches_oracle():
             if p.is_alive():
                 p.kill()
     assert all(v == "ok" for v in res.values()), res
+
+
+def test_e2e_layer_groups_partition_the_layouts():
+    """The one-GPU e2e pipelines by layer groups: every tensor of both layouts lands in exactly one
+    group, the embedding with the first layers and the head and final norm with the last."""
+    cfg = bench.workload(1, 8)
+    spl, tpl = cfg.layouts()
+    for per in (1, 3):
+        groups = bench.layer_groups(spl, tpl, per)
+        assert len(groups) == -(-8 // per)
+        for which, lay in ((0, spl), (1, tpl)):
+            for r, metas in lay.layout.items():
+                names = [n for g in groups for n in g[which].layout[r]]
+                assert sorted(names) == sorted(metas), (per, which, r)
+        assert "wte.weight" in groups[0][0].layout[0] and "lm_head.weight" in groups[-1][0].layout[0]
+        assert "norm.weight" in groups[-1][1].layout[1]
+
+
+def test_reference_arm_plans_without_the_product_library():
+    """The reference arm's sample is planned by the oracle; nothing loads libsuika_reshard.so (in a
+    fresh process: other tests of this session load it)."""
+    import subprocess
+    import sys
+    code = ("import sys; sys.argv = ['bench.py']; import bench; "
+            "smp = bench.OracleSample(bench.workload(1, 1), 1, 2); "
+            "print(smp.units, smp.ranks, 'libsuika_reshard' in open('/proc/self/maps').read())")
+    out = subprocess.run([sys.executable, "-c", code], cwd=os.path.dirname(os.path.abspath(bench.__file__)),
+                         capture_output=True, text=True, timeout=300)
+    assert out.returncode == 0, out.stderr
+    assert out.stdout.split() == ["866123776", "[0,", "1]", "False"], out.stdout
+
+
+def test_result_config_is_the_same_for_both_arms():
+    for n in (1, 8):
+        cfg = bench.workload(n)
+        assert bench.workload_config(cfg, n) == bench.workload_config(bench.workload(n), n)
+    assert "cfg2b" in bench.workload_config(bench.workload(1), 1)["workload"]
