@@ -78,3 +78,49 @@ def test_reference_errors_are_the_reference_exceptions():
         RM.schedule_param_transfer(rspl, rtpl)
     with pytest.raises(AssertionError):
         M.Plan(rspl, rtpl)
+
+
+def _functions_calling(tree, callee):
+    import ast
+    out = {}
+    for node in ast.walk(tree):
+        if isinstance(node, ast.FunctionDef):
+            calls = [c for c in ast.walk(node) if isinstance(c, ast.Call) and isinstance(c.func, ast.Name) and c.func.id == callee]
+            if calls:
+                out[node.name] = calls
+    return out
+
+
+def test_public_api_reaches_the_drop_in_through_module_globals():
+    """migration_save and migration_load (Suika/migration.py:1357,1546) call
+    schedule_and_execute_param_transfer, and the IPC hand-off functions, by their module-level
+    names, so rebinding those globals (the switch INTEGRATION.md describes) reroutes both paths;
+    and every keyword they pass is a parameter of the drop-in."""
+    import ast
+    import inspect
+    RM = _ref()
+    tree = ast.parse(inspect.getsource(RM))
+    callers = _functions_calling(tree, "schedule_and_execute_param_transfer")
+    assert {"migration_save", "migration_load"} <= set(callers)
+    params = list(inspect.signature(M.schedule_and_execute_param_transfer).parameters)
+    for fn in ("migration_save", "migration_load"):
+        for call in callers[fn]:
+            assert {kw.arg for kw in call.keywords} <= set(params), fn
+    ref_params = list(inspect.signature(RM.schedule_and_execute_param_transfer).parameters)
+    assert params[:len(ref_params)] == ref_params  # the reference's parameters, in its order
+    from suika_b200 import handoff as H
+    for name, fn in (("interactive_IPC_state_dict_send", H.interactive_IPC_state_dict_send),
+                     ("interactive_IPC_state_dict_recv", H.interactive_IPC_state_dict_recv)):
+        sites = _functions_calling(tree, name)
+        assert {"migration_save", "migration_load"} & set(sites), name
+        ours = set(inspect.signature(fn).parameters)
+        for calls in sites.values():
+            for call in calls:
+                assert {kw.arg for kw in call.keywords} <= ours, name
+    # the rebinding takes: the reference module resolves the name at call time
+    orig = RM.schedule_and_execute_param_transfer
+    try:
+        RM.schedule_and_execute_param_transfer = M.schedule_and_execute_param_transfer
+        assert RM.__dict__["schedule_and_execute_param_transfer"] is M.schedule_and_execute_param_transfer
+    finally:
+        RM.schedule_and_execute_param_transfer = orig
