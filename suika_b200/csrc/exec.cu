@@ -490,24 +490,29 @@ __global__ void __launch_bounds__(32, MINB) rs_copy_tma_kernel(const DevSeg* __r
 }
 
 // ---------------------------------------------------------------------------------------------
-// Tensor-map variant: 2-D TMA boxes through a shared-memory ring (SUIKA_RS_VARIANT 9-14).
-// Every local, 16-byte aligned entry is described to the TMA unit as two 2-D tensors of 8-byte
-// elements, its source and its target, each (row_bytes / 8) x rows with its own pitch; one
-// cp.async.bulk.tensor.2d load moves a box of up to 2 KB x box_h rows (a whole strided tile) into
-// a shared-memory stage, and one cp.async.bulk.tensor.2d store writes it to the target. The TMA
+// Tensor-map variant: TMA boxes through a shared-memory ring (SUIKA_RS_VARIANT 9-14).
+// Every local, 16-byte aligned entry is described to the TMA unit as two tensors of 8-byte
+// elements, its source and its target, each its rows with their own pitch; one
+// cp.async.bulk.tensor.3d load moves a box (whole rows, or a 2 KB-wide strided tile) into a
+// shared-memory stage, and one cp.async.bulk.tensor.3d store writes it to the target. The TMA
 // unit clips boxes at the tensor edges, so ragged tiles need no code. One thread per CTA issues
 // everything; STAGES - 1 loads stay in flight behind the store being issued. Entries that do not
 // qualify (remote, or not 16-byte aligned) are left to the vector-copy kernel in the same run.
 // Tensor maps never describe another GPU's memory here and no load uses cluster multicast.
 // ---------------------------------------------------------------------------------------------
+// The maps are 3-D: (x, chunk, row). A row that divides into n equal chunks of c bytes (16 | c,
+// 256 <= c <= 2 KB, n <= 256) is seen as (c / 8, n, rows) and a box spans whole rows, or as many
+// chunks of one row as a stage holds; any other row is (row_bytes / 8, 1, rows) with boxes of up
+// to 2 KB across it. Box k of a row band starts at x = k * xstep, chunk = k * ystep.
 struct alignas(64) TensorEntry {
-  CUtensorMap src;      // 2-D map of the source: (row_bytes / 8, rows), pitch = source pitch
-  CUtensorMap dst;      // 2-D map of the target: (row_bytes / 8, rows), pitch = target pitch
+  CUtensorMap src;      // map of the source rows (pitch = source pitch)
+  CUtensorMap dst;      // map of the target rows (pitch = target pitch)
   uint64_t tile_begin;  // global index of this entry's first box
   uint32_t col_boxes;   // boxes across a row
-  uint32_t box_w;       // box width in 8-byte elements (even: x * 8 stays 16-byte aligned)
+  uint32_t xstep;       // x of box k = k * xstep (8-byte elements; even, so x * 8 stays 16-byte aligned)
+  uint32_t ystep;       // chunk of box k = k * ystep
   uint32_t box_h;       // box height in rows
-  uint32_t box_bytes;   // box_w * 8 * box_h: the bytes a box load always delivers to shared memory
+  uint32_t box_bytes;   // bytes a box load always delivers to shared memory (the whole box)
   // Entries that are column slices of the same source rows (the pieces of a TP grow) form a group
   // of consecutive entries with one geometry and one tile_begin; the group's boxes are numbered
   // row band by row band across its members, so CTAs that run at the same time read whole source
@@ -517,13 +522,15 @@ struct alignas(64) TensorEntry {
 };
 static_assert(sizeof(TensorEntry) == 320, "TensorEntry layout");
 
-__device__ __forceinline__ void tma_load_2d(uint32_t smem_dst, const CUtensorMap* map, int32_t x, int32_t y, uint32_t bar) {
-  asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
-               ::"r"(smem_dst), "l"(map), "r"(x), "r"(y), "r"(bar) : "memory");
+__device__ __forceinline__ void tma_load_3d(uint32_t smem_dst, const CUtensorMap* map, int32_t x, int32_t y, int32_t z,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
+      ::"r"(smem_dst), "l"(map), "r"(x), "r"(y), "r"(z), "r"(bar) : "memory");
 }
-__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, int32_t x, int32_t y, uint32_t smem_src) {
-  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%1, %2}], [%3];"
-               ::"l"(map), "r"(x), "r"(y), "r"(smem_src) : "memory");
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, int32_t x, int32_t y, int32_t z, uint32_t smem_src) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%1, %2, %3}], [%4];"
+               ::"l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_src) : "memory");
 }
 // The same with an L2 cache policy (evict-first: every byte is read once and written once).
 __device__ __forceinline__ uint64_t l2_evict_first_policy() {
@@ -531,15 +538,17 @@ __device__ __forceinline__ uint64_t l2_evict_first_policy() {
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
   return p;
 }
-__device__ __forceinline__ void tma_load_2d_hint(uint32_t smem_dst, const CUtensorMap* map, int32_t x, int32_t y, uint32_t bar,
-                                                 uint64_t policy) {
+__device__ __forceinline__ void tma_load_3d_hint(uint32_t smem_dst, const CUtensorMap* map, int32_t x, int32_t y, int32_t z,
+                                                 uint32_t bar, uint64_t policy) {
   asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%2, %3}], [%4], %5;"
-      ::"r"(smem_dst), "l"(map), "r"(x), "r"(y), "r"(bar), "l"(policy) : "memory");
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%2, %3, %4}], "
+      "[%5], %6;"
+      ::"r"(smem_dst), "l"(map), "r"(x), "r"(y), "r"(z), "r"(bar), "l"(policy) : "memory");
 }
-__device__ __forceinline__ void tma_store_2d_hint(const CUtensorMap* map, int32_t x, int32_t y, uint32_t smem_src, uint64_t policy) {
-  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group.L2::cache_hint [%0, {%1, %2}], [%3], %4;"
-               ::"l"(map), "r"(x), "r"(y), "r"(smem_src), "l"(policy) : "memory");
+__device__ __forceinline__ void tma_store_3d_hint(const CUtensorMap* map, int32_t x, int32_t y, int32_t z, uint32_t smem_src,
+                                                  uint64_t policy) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group.L2::cache_hint [%0, {%1, %2, %3}], [%4], %5;"
+               ::"l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_src), "l"(policy) : "memory");
 }
 // The maps were written to global memory by a host copy before the launch; acquire them for the
 // tensor-map proxy before their first use.
@@ -580,7 +589,7 @@ __global__ void __launch_bounds__(32, 1) rs_copy_tensor_kernel(const TensorEntry
   if (threadIdx.x != 0) return;
   struct Slot {
     const CUtensorMap* dst;
-    int32_t x, y;
+    int32_t x, y, z;
   };
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;  // stage buffers start 1 KB aligned
@@ -619,15 +628,16 @@ __global__ void __launch_bounds__(32, 1) rs_copy_tensor_kernel(const TensorEntry
     const uint32_t s = (uint32_t)(issued % STAGES);
     Slot& sl = slots[s];
     sl.dst = &e.dst;
-    sl.x = (int32_t)(cb * e.box_w);
-    sl.y = (int32_t)(rb * e.box_h);
+    sl.x = (int32_t)(cb * e.xstep);
+    sl.y = (int32_t)(cb * e.ystep);
+    sl.z = (int32_t)(rb * e.box_h);
     const uint32_t bar = smem_u32(&bars[s]);
     mbar_arrive_expect_tx(bar, e.box_bytes);
     // RS_RUN_STALL_FIRST_STAGE (tests of the error path): the first box's barrier expects bytes
     // that no load delivers, so its bounded wait runs out; nothing is in flight into that stage.
     if (!(stall_first && issued == 0)) {
-      if (EVICT_FIRST) tma_load_2d_hint(base + s * (uint32_t)STAGE_BYTES, &e.src, sl.x, sl.y, bar, policy);
-      else tma_load_2d(base + s * (uint32_t)STAGE_BYTES, &e.src, sl.x, sl.y, bar);
+      if (EVICT_FIRST) tma_load_3d_hint(base + s * (uint32_t)STAGE_BYTES, &e.src, sl.x, sl.y, sl.z, bar, policy);
+      else tma_load_3d(base + s * (uint32_t)STAGE_BYTES, &e.src, sl.x, sl.y, sl.z, bar);
     }
     ++issued;
   };
@@ -641,8 +651,8 @@ __global__ void __launch_bounds__(32, 1) rs_copy_tensor_kernel(const TensorEntry
       failed = true;
       break;
     }
-    if (EVICT_FIRST) tma_store_2d_hint(slots[s].dst, slots[s].x, slots[s].y, base + s * (uint32_t)STAGE_BYTES, policy);
-    else tma_store_2d(slots[s].dst, slots[s].x, slots[s].y, base + s * (uint32_t)STAGE_BYTES);
+    if (EVICT_FIRST) tma_store_3d_hint(slots[s].dst, slots[s].x, slots[s].y, slots[s].z, base + s * (uint32_t)STAGE_BYTES, policy);
+    else tma_store_3d(slots[s].dst, slots[s].x, slots[s].y, slots[s].z, base + s * (uint32_t)STAGE_BYTES);
     bulk_commit();
     if (issued < n) {
       // the new box goes into the stage of box k - 1, whose store must have read it out
@@ -876,13 +886,14 @@ bool tensor_desc(const rs_copy_desc& d) {
   return d.rows < (1ull << 31) && d.row_bytes / 8 <= (1ull << 32);
 }
 
-int encode_2d(EncodeTiledFn fn, CUtensorMap* m, uint64_t addr, uint64_t cols, uint64_t rows, uint64_t pitch, uint32_t bw,
-              uint32_t bh) {
-  const cuuint64_t dims[2] = {cols, rows};
-  const cuuint64_t strides[1] = {pitch};
-  const cuuint32_t box[2] = {bw, bh};
-  const cuuint32_t elem_strides[2] = {1, 1};
-  const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, reinterpret_cast<void*>(addr), dims, strides, box, elem_strides,
+// A 3-D map of 8-byte elements: dims (x, chunk, row), strides in bytes (chunk, row).
+int encode_3d(EncodeTiledFn fn, CUtensorMap* m, uint64_t addr, const uint64_t dim[3], uint64_t chunk_stride, uint64_t pitch,
+              const uint32_t box[3]) {
+  const cuuint64_t dims[3] = {dim[0], dim[1], dim[2]};
+  const cuuint64_t strides[2] = {chunk_stride, pitch};
+  const cuuint32_t boxd[3] = {box[0], box[1], box[2]};
+  const cuuint32_t elem_strides[3] = {1, 1, 1};
+  const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, reinterpret_cast<void*>(addr), dims, strides, boxd, elem_strides,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return efail(RS_ERR_CUDA, "rs_copy_stage: cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
@@ -894,30 +905,56 @@ struct TensorGeom {
   uint64_t src, src_pitch, rows, row_bytes;
 };
 
-// One rows x row_bytes rectangle -> one TensorEntry, its boxes numbered from `ntiles`. Boxes are
-// 2 KB wide (256 elements; a narrower row gets one box as wide as the row, rounded up to an even
-// element count) so that every box but a row's last starts and ends on 128-byte lines, and as tall
-// as the stage holds.
+// One rows x row_bytes rectangle -> one TensorEntry, its boxes numbered from `ntiles`. A row that
+// splits into equal chunks (see TensorEntry) gets boxes of whole rows, as many as a stage holds,
+// so loads read and stores write whole rows; a row longer than a stage gets boxes of as many of
+// its chunks as fit. Any other row gets boxes 2 KB wide (a narrower row: one box as wide as the
+// row, rounded up to an even element count) and as tall as the stage holds.
 int add_tensor_entry(EncodeTiledFn fn, uint64_t src, uint64_t dst, uint64_t rows, uint64_t row_bytes, uint64_t sp, uint64_t dp,
                      uint32_t stage_bytes, uint64_t& ntiles, std::vector<TensorEntry>& out, std::vector<TensorGeom>& geom) {
   const uint64_t cols = row_bytes / 8;
-  uint64_t bw = std::min<uint64_t>(cols, 256);
-  bw += bw & 1;
-  const uint64_t bh = std::min<uint64_t>(std::min<uint64_t>(rows, 256), std::max<uint64_t>(1, stage_bytes / (bw * 8)));
   if (rows == 1) sp = dp = (row_bytes + 15) & ~15ull;  // one row: the stride only has to be legal
+  uint64_t chunk = 0;  // whole-row boxes: the widest chunk c dividing the row with 16 | c and n <= 256
+  for (uint64_t c = std::min<uint64_t>(2048, row_bytes) & ~15ull; c >= 256; c -= 16)
+    if (row_bytes % c == 0 && row_bytes / c <= 256) {
+      chunk = c;
+      break;
+    }
+  uint64_t dim[3];
+  uint32_t box[3];
+  uint64_t chunk_stride;
   TensorEntry te;
   std::memset(&te, 0, sizeof(te));
-  te.col_boxes = (uint32_t)((cols + bw - 1) / bw);
-  te.box_w = (uint32_t)bw;
-  te.box_h = (uint32_t)bh;
-  te.box_bytes = (uint32_t)(bw * 8 * bh);
+  if (chunk) {
+    const uint64_t n = row_bytes / chunk;
+    const uint64_t bn = row_bytes <= stage_bytes ? n : std::max<uint64_t>(1, stage_bytes / chunk);
+    const uint64_t bh = row_bytes <= stage_bytes ? std::min<uint64_t>(std::min<uint64_t>(rows, 256), stage_bytes / row_bytes) : 1;
+    dim[0] = chunk / 8; dim[1] = n; dim[2] = rows;
+    box[0] = (uint32_t)(chunk / 8); box[1] = (uint32_t)bn; box[2] = (uint32_t)bh;
+    chunk_stride = chunk;
+    te.col_boxes = (uint32_t)((n + bn - 1) / bn);
+    te.xstep = 0;
+    te.ystep = (uint32_t)bn;
+  } else {  // boxes of up to 2 KB across the row (an even element count, so x stays 16-byte aligned)
+    uint64_t bw = std::min<uint64_t>(cols, 256);
+    bw += bw & 1;
+    const uint64_t bh = std::min<uint64_t>(std::min<uint64_t>(rows, 256), std::max<uint64_t>(1, stage_bytes / (bw * 8)));
+    dim[0] = cols; dim[1] = 1; dim[2] = rows;
+    box[0] = (uint32_t)bw; box[1] = 1; box[2] = (uint32_t)bh;
+    chunk_stride = (row_bytes + 15) & ~15ull;
+    te.col_boxes = (uint32_t)((cols + bw - 1) / bw);
+    te.xstep = (uint32_t)bw;
+    te.ystep = 0;
+  }
+  te.box_h = box[2];
+  te.box_bytes = box[0] * 8 * box[1] * box[2];
   te.tile_begin = ntiles;
   te.group = 1;
   te.member = 0;
-  int rc = encode_2d(fn, &te.src, src, cols, rows, sp, (uint32_t)bw, (uint32_t)bh);
-  if (!rc) rc = encode_2d(fn, &te.dst, dst, cols, rows, dp, (uint32_t)bw, (uint32_t)bh);
+  int rc = encode_3d(fn, &te.src, src, dim, chunk_stride, sp, box);
+  if (!rc) rc = encode_3d(fn, &te.dst, dst, dim, chunk_stride, dp, box);
   if (rc) return rc;
-  ntiles += (uint64_t)te.col_boxes * ((rows + bh - 1) / bh);
+  ntiles += (uint64_t)te.col_boxes * ((rows + te.box_h - 1) / te.box_h);
   out.push_back(te);
   geom.push_back(TensorGeom{src, sp, rows, row_bytes});
   return RS_OK;
