@@ -741,9 +741,16 @@ def main():
     ap.add_argument("--peer-variants", default="2,6")
     ap.add_argument("--peer-one", action="store_true",
                     help="with --peer-probe: one pull launch then one push launch on GPU 0 against GPU 1 (for a profiler)")
+    ap.add_argument("--pack-probe", action="store_true",
+                    help="time the copy kernel's one-GPU patterns (column slices of one source, one contiguous run) instead")
+    ap.add_argument("--pack-gib", type=float, default=8.0)
+    ap.add_argument("--pack-variants", default="8,9,11,14")
     args = ap.parse_args()
     if args.peer_probe:
         run_peer_probe(args)
+        return
+    if args.pack_probe:
+        run_pack_probe(args)
         return
     if args.checkpoint:
         print(json.dumps(run_checkpoint(args)), flush=True)
@@ -966,6 +973,60 @@ def run_peer_probe(args):
                 ms = _peer_time(cfg)
                 print(f"variant {var} {'strided' if st else 'contig '} {name:18s}: {ms:7.3f} ms  "
                       f"{moved / ms / 1e6:6.0f} GB/s per direction", flush=True)
+
+
+# ---------------------------------------------------------------------------------------------
+# --pack-probe: one-GPU copy patterns (one process)
+# ---------------------------------------------------------------------------------------------
+def _median_event_s(fn, reps=10):
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+    for a, b in evs:
+        a.record()
+        fn()
+        b.record()
+    torch.cuda.synchronize()
+    return float(np.median([a.elapsed_time(b) for a, b in evs])) / 1e3
+
+
+def run_pack_probe(args):
+    """One-GPU patterns of a relayout, per launch shape (SUIKA_RS_VARIANT): the two column slices
+    of one source matrix, each slice row_bytes wide at a pitch of twice that, written to two
+    contiguous targets (the TP-grow pieces of a row-parallel weight: 22016 bytes is an fp32
+    Llama2-7B down_proj half-row, 11008 its bf16 copy, 8192 an fp32 o_proj half-row), and one
+    contiguous run. The buffer is larger than L2; rates are read + write bytes over the median
+    CUDA-event time of 10 launches, beside torch's own copy of the whole buffer."""
+    dev = torch.device("cuda", 0)
+    n = int(args.pack_gib * (1 << 30)) & ~((1 << 20) - 1)
+    src = torch.randint(0, 255, (n,), dtype=torch.uint8, device=dev)
+    dst = torch.empty(n, dtype=torch.uint8, device=dev)
+    t = _median_event_s(lambda: dst.copy_(src))
+    print(f"torch copy_: {2 * n / t / 1e9:.0f} GB/s", flush=True)
+    pats = {}
+    for rb in (22016, 11008, 8192, 4096):
+        rows = n // (2 * rb)
+        pats[f"halves {rb}/{2 * rb}"] = [(src.data_ptr() + h * rb, dst.data_ptr() + h * (n // 2), rows, rb, 2 * rb, rb, 0)
+                                         for h in (0, 1)]
+    pats["contiguous"] = [(src.data_ptr(), dst.data_ptr(), 1, n, n, n, 0)]
+    for v in args.pack_variants.split(","):
+        os.environ["SUIKA_RS_VARIANT"] = v
+        for name, descs in pats.items():
+            moved = sum(d[2] * d[3] for d in descs)
+            dst.zero_()
+            p = M.PreparedCopies(np.array(descs, dtype=M.L.COPY_DESC_DTYPE), dev)
+            t = _median_event_s(p.launch)
+            p.check()
+            d0 = descs[0]
+            got = dst[:d0[2] * d0[3]].view(d0[2], d0[3])[::997]
+            want = src[:d0[2] * d0[4]].view(d0[2], d0[4])[::997, :d0[3]]
+            if not torch.equal(got, want):
+                raise RuntimeError(f"variant {v} {name}: target differs from source")
+            print(f"variant {v:>2} {name:22s}: {t * 1e3:7.3f} ms {2 * moved / t / 1e9:6.0f} GB/s  "
+                  f"(vector entries {p.info.n_entries}, tensor-map entries {p.info.n_tensor_entries}, boxes {p.info.n_tensor_tiles})",
+                  flush=True)
+            del p
 
 
 # ---------------------------------------------------------------------------------------------

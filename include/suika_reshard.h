@@ -268,8 +268,9 @@ typedef struct rs_launch_info {
   int32_t variant;         /* launch shape (SUIKA_RS_VARIANT - 1)      */
   int32_t reserved;
   /* Tensor-map launch shapes (SUIKA_RS_VARIANT 9-14): the local, 16-byte aligned entries go to a
-   * kernel that moves 2-D boxes with cp.async.bulk.tensor (one load and one store per box of up
-   * to 2 KB x rows); the fields above then describe the other entries, run by the vector copy. */
+   * kernel that moves 3-D boxes with cp.async.bulk.tensor (one load and one store per box of
+   * whole rows, or up to 2 KB x rows); the fields above then describe the other entries, run by
+   * the vector copy. */
   int64_t n_tensor_entries; /* entries (tensor-map pairs) of the tensor-map kernel */
   uint64_t n_tensor_tiles;  /* boxes it moves                                      */
   int32_t tensor_grid;      /* its CTAs                                             */
@@ -322,7 +323,7 @@ int rs_copy_launch(const rs_copy_desc* descs, int64_t n_desc,
  * until the process exits). It calls no cudaMalloc, cudaFree or other allocating routine.
  *   - Larger tables are rejected with RS_ERR_CAPACITY; use rs_copy_launch for them.
  *   - The first call on a device looks up the array's device address (cudaGetSymbolAddress)
- *     with that device current. Make that first call before any stream capture.
+ *     with that device current.
  *   - Every call shares the one array and overwrites the entries it uses; nothing in it needs
  *     to start at zero. Calls on the same stream are ordered; calls that overlap on the GPU
  *     (different streams, or several threads) race on the array.

@@ -112,12 +112,31 @@ def _resolve(src: _Stage, dst: _Stage, geo: L.RsActGeometry, pieces: np.ndarray,
     return out
 
 
+def rotated_pieces(pieces: np.ndarray, rank: int) -> np.ndarray:
+    """The pieces `rank` sends, ordered so that the senders start at different receivers.
+
+    The copy kernel's CTAs walk the table in order, so a sender's bytes leave one receiver at a
+    time. Had every sender the same receiver order, all of them would write to the first
+    receiver together, two or more links into one ingress, while the others idled. Sender i of
+    n (ascending rank) starts instead at receiver i * m // n of the m receivers and goes round:
+    with n == m each receiver has one writer at a time. The order within a receiver is kept."""
+    mine = pieces[pieces["src_rank"] == rank]
+    senders = sorted(set(pieces["src_rank"].tolist()))
+    receivers = sorted(set(pieces["dst_rank"].tolist()))
+    if len(mine) < 2 or len(receivers) < 2:
+        return mine
+    start = senders.index(rank) * len(receivers) // len(senders)
+    turn = {r: (i - start) % len(receivers) for i, r in enumerate(receivers)}
+    keys = np.array([turn[int(r)] for r in mine["dst_rank"]])
+    return mine[np.argsort(keys, kind="stable")]
+
+
 def send_table(src: _Stage, dst: _Stage, geo: L.RsActGeometry, pieces: np.ndarray, rank: int,
                activation_ptr: int, windows: Dict[int, int]) -> np.ndarray:
     """What a sending rank writes in one exchange: its blocks, from its activation at
     activation_ptr into each receiver's window slot (windows: receiver rank -> slot address in
-    this process), laid out as the receiver's tensor."""
-    mine = pieces[pieces["src_rank"] == rank]
+    this process), laid out as the receiver's tensor, receivers in rotated_pieces' order."""
+    mine = rotated_pieces(pieces, rank)
     return _resolve(src, dst, geo, mine, {rank: activation_ptr}, {r: windows[r] for r in set(mine["dst_rank"].tolist())})
 
 

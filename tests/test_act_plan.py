@@ -191,3 +191,45 @@ def test_random_exchanges_match_the_oracle(k):
     _apply(mem, A._resolve(src, dst, _geo(case, 4), pieces, sa, da))
     for r in tgts:
         assert np.array_equal(tgts[r], want[r]), r
+
+
+def _turns(pieces):
+    """For each sender, its receivers in send order (one entry per receiver, first visit)."""
+    out = {}
+    for s in sorted(set(pieces["src_rank"].tolist())):
+        seen = []
+        for r in A.rotated_pieces(pieces, s)["dst_rank"].tolist():
+            if r not in seen:
+                seen.append(int(r))
+        out[s] = seen
+    return out
+
+
+@pytest.mark.parametrize("k", range(40))
+def test_rotated_send_order_is_a_permutation(k):
+    """rotated_pieces only reorders: each sender keeps exactly its own pieces, and the pieces of
+    one receiver stay together in their planner order."""
+    case = random_act_cases()[k]
+    src, dst = _stages(case)
+    pieces = A._plan(src, dst, _slice_size(case))
+    for s in set(pieces["src_rank"].tolist()):
+        mine = pieces[pieces["src_rank"] == s]
+        rot = A.rotated_pieces(pieces, s)
+        assert sorted(map(tuple, rot.tolist())) == sorted(map(tuple, mine.tolist()))
+        for r in set(mine["dst_rank"].tolist()):
+            assert rot[rot["dst_rank"] == r].tolist() == mine[mine["dst_rank"] == r].tolist()
+        firsts = [i for i, r in enumerate(rot["dst_rank"].tolist()) if i == 0 or rot["dst_rank"][i - 1] != r]
+        assert len(firsts) == len(set(rot["dst_rank"].tolist())), "a receiver's pieces are split"
+
+
+@pytest.mark.parametrize("tp", [2, 4])
+def test_rotated_send_order_gives_each_receiver_one_writer(tp):
+    """A TP group handing over to as many DP ranks, and back: at every turn of the send order
+    each receiver is written by exactly one sender (the stage pairs of bench.py --activation)."""
+    ma, mb = [list(range(tp))], [[tp + i] for i in range(tp)]
+    ba, bb = [8], [8 // tp] * tp
+    for ms, md, bs, bd in ((ma, mb, ba, bb), (mb, ma, bb, ba)):
+        pieces = A.plan_activation_exchange(ms, md, bs, bd, 5120)
+        turns = _turns(pieces)
+        for t in range(tp):
+            assert sorted(order[t] for order in turns.values()) == sorted(set(pieces["dst_rank"].tolist())), (ms, md, turns)
