@@ -992,11 +992,12 @@ def _median_event_s(fn, reps=10):
 
 
 def run_pack_probe(args):
-    """One-GPU patterns of a relayout, per launch shape (SUIKA_RS_VARIANT): the two column slices
-    of one source matrix, each slice row_bytes wide at a pitch of twice that, written to two
-    contiguous targets (the TP-grow pieces of a row-parallel weight: 22016 bytes is an fp32
-    Llama2-7B down_proj half-row, 11008 its bf16 copy, 8192 an fp32 o_proj half-row), and one
-    contiguous run. The buffer is larger than L2; rates are read + write bytes over the median
+    """One-GPU patterns of a relayout, per launch shape (SUIKA_RS_VARIANT). A "halves" pattern is
+    the TP-grow pieces of row-parallel weights: source matrices of 4096 rows (Llama2-7B's hidden
+    size) with rows of twice row_bytes, each cut into its two column slices, written to two
+    contiguous targets, as many matrices as the buffer holds (22016-byte slices are fp32 down_proj
+    half-rows, 11008 their bf16 copy, 8192 fp32 o_proj half-rows). "contiguous" is one run over
+    the whole buffer. The buffer is larger than L2; rates are read + write bytes over the median
     CUDA-event time of 10 launches, beside torch's own copy of the whole buffer."""
     dev = torch.device("cuda", 0)
     n = int(args.pack_gib * (1 << 30)) & ~((1 << 20) - 1)
@@ -1004,11 +1005,15 @@ def run_pack_probe(args):
     dst = torch.empty(n, dtype=torch.uint8, device=dev)
     t = _median_event_s(lambda: dst.copy_(src))
     print(f"torch copy_: {2 * n / t / 1e9:.0f} GB/s", flush=True)
+    rows = 4096
     pats = {}
     for rb in (22016, 11008, 8192, 4096):
-        rows = n // (2 * rb)
-        pats[f"halves {rb}/{2 * rb}"] = [(src.data_ptr() + h * rb, dst.data_ptr() + h * (n // 2), rows, rb, 2 * rb, rb, 0)
-                                         for h in (0, 1)]
+        mat = rows * 2 * rb
+        descs = []
+        for m in range(n // mat):
+            for h in (0, 1):
+                descs.append((src.data_ptr() + m * mat + h * rb, dst.data_ptr() + m * mat + h * rows * rb, rows, rb, 2 * rb, rb, 0))
+        pats[f"halves {rb}/{2 * rb} x{n // mat}"] = descs
     pats["contiguous"] = [(src.data_ptr(), dst.data_ptr(), 1, n, n, n, 0)]
     for v in args.pack_variants.split(","):
         os.environ["SUIKA_RS_VARIANT"] = v
@@ -1018,12 +1023,13 @@ def run_pack_probe(args):
             p = M.PreparedCopies(np.array(descs, dtype=M.L.COPY_DESC_DTYPE), dev)
             t = _median_event_s(p.launch)
             p.check()
-            d0 = descs[0]
-            got = dst[:d0[2] * d0[3]].view(d0[2], d0[3])[::997]
-            want = src[:d0[2] * d0[4]].view(d0[2], d0[4])[::997, :d0[3]]
-            if not torch.equal(got, want):
-                raise RuntimeError(f"variant {v} {name}: target differs from source")
-            print(f"variant {v:>2} {name:22s}: {t * 1e3:7.3f} ms {2 * moved / t / 1e9:6.0f} GB/s  "
+            for d in (descs[0], descs[-1]):
+                got = torch.empty(d[2] * d[3], dtype=torch.uint8, device=dev)
+                got.copy_(dst[d[1] - dst.data_ptr():][:d[2] * d[3]])
+                want = src[d[0] - src.data_ptr():][:(d[2] - 1) * d[4] + d[3]].as_strided((d[2], d[3]), (d[4], 1))
+                if not torch.equal(got.view(d[2], d[3]), want):
+                    raise RuntimeError(f"variant {v} {name}: target differs from source")
+            print(f"variant {v:>2} {name:26s}: {t * 1e3:7.3f} ms {2 * moved / t / 1e9:6.0f} GB/s  "
                   f"(vector entries {p.info.n_entries}, tensor-map entries {p.info.n_tensor_entries}, boxes {p.info.n_tensor_tiles})",
                   flush=True)
             del p

@@ -672,7 +672,8 @@ __global__ void __launch_bounds__(32, 1) rs_copy_tensor_kernel(const TensorEntry
 // Launch shapes. Vector-copy variants: (threads per CTA, 16-byte loads in flight per thread, CTAs
 // per SM), each with 64 KB of loads in flight per SM; on cfg2b (1 x B200, 128 KB tiles) they span
 // 5.83-6.00 TB/s. TMA variants: one warp per CTA, (stages, stage bytes, stages in flight, CTAs per
-// SM). The default (SUIKA_RS_VARIANT=2: 256 x 8 x 2) keeps two CTAs per SM.
+// SM). Unset, SUIKA_RS_VARIANT picks shape 8 or 2 per table (kAutoLocalVariant / kAutoRemoteVariant
+// below); both are 256 x 8 with two CTAs per SM.
 struct Variant {
   int block, unroll, min_blocks;
   size_t smem;
@@ -1324,8 +1325,8 @@ int noalloc_table_addr(int dev, DevSeg** out) {
 }
 
 // The no-allocation launch runs only the vector-copy kernels: they have no waits, so there is no
-// status a caller would have to read back. A TMA variant selected by SUIKA_RS_VARIANT falls back
-// to the default launch shape.
+// status a caller would have to read back. Unset, or set to a TMA variant, SUIKA_RS_VARIANT gives
+// the vector shape 2 here.
 int noalloc_variant() {
   const int v = selected_variant();
   return (v != kAutoVariant && !is_tensor_variant(v) && kVariants[v].smem == 0) ? v : 1;
