@@ -490,7 +490,7 @@ __global__ void __launch_bounds__(32, MINB) rs_copy_tma_kernel(const DevSeg* __r
 }
 
 // ---------------------------------------------------------------------------------------------
-// Tensor-map variant: TMA boxes through a shared-memory ring (SUIKA_RS_VARIANT 9-14).
+// Tensor-map variant: TMA boxes through a shared-memory ring (SUIKA_RS_VARIANT 9-15).
 // Every local, 16-byte aligned entry is described to the TMA unit as two tensors of 8-byte
 // elements, its source and its target, each its rows with their own pitch; one
 // cp.async.bulk.tensor.3d load moves a box (whole rows, or a 2 KB-wide strided tile) into a
@@ -693,22 +693,25 @@ const Variant kVariants[] = {
     {256, 8, 2, 0, rs_copy_kernel<256, 8, 2, true>},  // 8: variant 2 with streaming cache hints
 };
 constexpr int kNumVariants = sizeof(kVariants) / sizeof(kVariants[0]);
-constexpr int kTensorVectorVariant = 1;  // launch shape of the entries the tensor-map kernel leaves out
-
-// Tensor-map launch shapes (SUIKA_RS_VARIANT 9-14): (stages, stage bytes, evict-first hints); one warp per CTA, CTAs
-// per SM as shared memory allows (1 for about 192 KB of stages, 2 for about 96 KB).
+// Tensor-map launch shapes (SUIKA_RS_VARIANT 9-15): (stages, stage bytes, evict-first hints); one warp per CTA, CTAs
+// per SM as shared memory allows (1 for about 192 KB of stages, 2 for about 96 KB). `vector` is the
+// launch shape of the entries the tensor-map kernel leaves out; `wide_only` keeps it to the rows it
+// reads fastest (wide_desc), leaving the narrower ones to the banded vector copy.
 struct TensorShape {
   int stages, stage_bytes;
   size_t smem;
   void (*fn)(const TensorEntry*, int32_t, uint64_t, RunArgs);
+  int vector;
+  bool wide_only;
 };
 const TensorShape kTensorShapes[] = {
-    {8, 24576, tensor_smem_bytes<8, 24576>(), rs_copy_tensor_kernel<8, 24576, false>},
-    {4, 24576, tensor_smem_bytes<4, 24576>(), rs_copy_tensor_kernel<4, 24576, false>},
-    {4, 49152, tensor_smem_bytes<4, 49152>(), rs_copy_tensor_kernel<4, 49152, false>},
-    {6, 16384, tensor_smem_bytes<6, 16384>(), rs_copy_tensor_kernel<6, 16384, false>},
-    {8, 24576, tensor_smem_bytes<8, 24576>(), rs_copy_tensor_kernel<8, 24576, true>},   // 13: 9 with evict-first L2 hints
-    {4, 49152, tensor_smem_bytes<4, 49152>(), rs_copy_tensor_kernel<4, 49152, true>},   // 14: 11 with evict-first L2 hints
+    {8, 24576, tensor_smem_bytes<8, 24576>(), rs_copy_tensor_kernel<8, 24576, false>, 1, false},
+    {4, 24576, tensor_smem_bytes<4, 24576>(), rs_copy_tensor_kernel<4, 24576, false>, 1, false},
+    {4, 49152, tensor_smem_bytes<4, 49152>(), rs_copy_tensor_kernel<4, 49152, false>, 1, false},
+    {6, 16384, tensor_smem_bytes<6, 16384>(), rs_copy_tensor_kernel<6, 16384, false>, 1, false},
+    {8, 24576, tensor_smem_bytes<8, 24576>(), rs_copy_tensor_kernel<8, 24576, true>, 1, false},  // 13: 9 with evict-first L2 hints
+    {4, 49152, tensor_smem_bytes<4, 49152>(), rs_copy_tensor_kernel<4, 49152, true>, 1, false},  // 14: 11 with evict-first L2 hints
+    {4, 49152, tensor_smem_bytes<4, 49152>(), rs_copy_tensor_kernel<4, 49152, false>, 7, true},  // 15: 11 for wide rows, 8 for the rest
 };
 constexpr int kNumTensorShapes = sizeof(kTensorShapes) / sizeof(kTensorShapes[0]);
 
@@ -729,12 +732,13 @@ uint64_t env_u64(const char* name, uint64_t dflt) {
 
 // Launch shape chosen by SUIKA_RS_VARIANT (1-based): 0-based index below kNumVariants for the
 // vector and bulk-copy kernels, kNumVariants + i for tensor-map shape i. Unset (or 0) selects per
-// table: a table whose entries all stay in this GPU's memory runs the vector shape 8 (evict-first
-// stores; with its TP-grow slices band-interleaved it is the fastest on a one-GPU relayout); a
-// table with any entry that crosses NVLink runs the vector shape 2, whose CTAs interleave remote
-// and local tiles so both links stay busy.
+// table: a table whose entries all stay in this GPU's memory runs shape 15 (wide rows and long
+// runs through the tensor-map kernel, the other rows through the vector shape 8 with evict-first
+// stores and band-interleaved TP-grow slices: the fastest split on a one-GPU relayout); a table
+// with any entry that crosses NVLink, or reads host memory, runs the vector shape 2, whose CTAs
+// interleave remote and local tiles so both links stay busy.
 constexpr int kAutoVariant = -1;
-constexpr int kAutoLocalVariant = 7;
+constexpr int kAutoLocalVariant = 14;  // kNumVariants + 6: tensor-map shape 15
 constexpr int kAutoRemoteVariant = 1;
 int selected_variant() {
   const uint64_t v = env_u64("SUIKA_RS_VARIANT", 0);
@@ -742,6 +746,16 @@ int selected_variant() {
   return (int)std::min<uint64_t>(v - 1, kNumVariants + kNumTensorShapes - 1);
 }
 bool is_tensor_variant(int v) { return v >= kNumVariants; }
+// Launch shape of the vector-copy part of a run.
+int vector_variant_of(int v) { return is_tensor_variant(v) ? kTensorShapes[v - kNumVariants].vector : v; }
+
+// Rows the tensor-map kernel reads faster than the banded vector copy (one-GPU probe of column
+// slices of 4096-row matrices): half-rows wider than 8 KB, and contiguous runs of 1 MB or more.
+// Narrower half-rows (8 KB, 4 KB) go faster through the vector copy's row bands.
+bool wide_desc(const rs_copy_desc& d) {
+  const bool contiguous = d.rows == 1 || (d.src_pitch == d.row_bytes && d.dst_pitch == d.row_bytes);
+  return contiguous ? d.rows * d.row_bytes >= (1ull << 20) : d.row_bytes > 8192;
+}
 
 // cuTensorMapEncodeTiled, looked up once through the runtime (no link against libcuda).
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*, const cuuint64_t*,
@@ -1062,7 +1076,7 @@ int rs_copy_stage(const rs_copy_desc* descs, int64_t n_desc, void* workspace_dev
       int rc = make_entry(d, i, tile_bytes, ntiles, sg, "rs_copy_stage");  // validates the descriptor either way
       if (rc) return rc;
       total += d.rows * d.row_bytes;
-      if (tensor && tensor_desc(d)) {
+      if (tensor && tensor_desc(d) && (!kTensorShapes[variant - kNumVariants].wide_only || wide_desc(d))) {
         ntiles = sg.tile_begin;  // not a vector-copy entry after all
         if (!encode && (rc = encode_tiled_fn(&encode))) return rc;
         rc = make_tensor_entries(encode, d, (uint32_t)kTensorShapes[variant - kNumVariants].stage_bytes, ntensor_tiles, tensor_table,
@@ -1121,7 +1135,7 @@ int rs_copy_stage(const rs_copy_desc* descs, int64_t n_desc, void* workspace_dev
   if ((e = cudaGetDevice(&dev)) != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
   const uint64_t cap_per_sm = env_u64("SUIKA_RS_CTAS_PER_SM", 8);
-  const Variant& v = kVariants[tensor ? kTensorVectorVariant : variant];
+  const Variant& v = kVariants[vector_variant_of(variant)];
   if (!table.empty()) {
     if (v.smem > 0 &&
         (e = cudaFuncSetAttribute(v.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)v.smem)) != cudaSuccess)
@@ -1157,9 +1171,9 @@ int rs_copy_run_bounded(const void* workspace_dev, const rs_launch_info* info, v
   if (wait_limit_ns == 0) return efail(RS_ERR_ARG, "rs_copy_run_bounded: the wait limit must be positive");
   if (flags & ~(uint32_t)RS_RUN_STALL_FIRST_STAGE) return efail(RS_ERR_ARG, "rs_copy_run_bounded: unknown flag bits");
   const bool tensor = is_tensor_variant(info->variant);
-  const Variant& v = kVariants[tensor ? kTensorVectorVariant : info->variant];
+  const Variant& v = kVariants[vector_variant_of(info->variant)];
   if ((flags & RS_RUN_STALL_FIRST_STAGE) && !(tensor ? tensor_part : v.smem > 0))
-    return efail(RS_ERR_ARG, "rs_copy_run_bounded: RS_RUN_STALL_FIRST_STAGE needs a TMA launch shape (SUIKA_RS_VARIANT 5-7 or 9-14)");
+    return efail(RS_ERR_ARG, "rs_copy_run_bounded: RS_RUN_STALL_FIRST_STAGE needs a TMA launch shape (SUIKA_RS_VARIANT 5-7 or 9-15)");
   char* ws = static_cast<char*>(const_cast<void*>(workspace_dev));
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   RunArgs run;

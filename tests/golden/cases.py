@@ -11,6 +11,9 @@ _gpt_mini = scaled_spec(SPECS["gpt-6.7b"], name="gpt-mini", hidden=128, n_layers
 _qwen_mini = scaled_spec(SPECS["qwen2-7b"], name="qwen-mini", hidden=256, n_layers=4, n_heads=8, n_kv_heads=4, head_dim=32,
                          ffn=512, vocab=512)
 _odd = scaled_spec(SPECS["llama-small"], name="llama-odd", hidden=24, n_layers=3, n_heads=2, ffn=40, vocab=50)
+# narrow model, wide FFN: TP1 and TP2 shards of down_proj have rows above 8 KB (the rows the one-GPU
+# default gives to the tensor-map kernel), TP4 fp32 shards too
+_llama_wide = scaled_spec(SPECS["llama2-13b"], name="llama-wide", hidden=64, n_layers=2, n_heads=2, ffn=8704, vocab=64)
 # the model of the next-training-step check (tests/golden/make_next_step_golden.py)
 NEXT_STEP_SPEC = scaled_spec(SPECS["llama2-13b"], name="next-step", hidden=128, n_layers=2, n_heads=4, ffn=256, vocab=128)
 
@@ -44,6 +47,10 @@ CASES = {
                         "description": "Llama (reduced) TP1 on 1 -> TP2xDP2 on 4 (TP and DP grow from one rank)"},
     "qwen_grow_mini": {"config": _cfg("qwen_grow_mini", _qwen_mini, src=[[[0, 1]]], dst=[[[0, 1, 2, 3]]]),
                        "description": "Qwen2 (reduced, GQA 8/4 heads, QKV bias) TP2 -> TP4 (grow)"},
+    "wide_mini": {"config": _cfg("wide_mini", _llama_wide, src=[[[0]]], dst=[[[0, 1]]]),
+                  "description": "Llama (hidden 64, ffn 8704) TP1 -> TP2: column slices with 17408- and 8704-byte rows"},
+    "wide_shrink_mini": {"config": _cfg("wide_shrink_mini", _llama_wide, src=[[[0, 1, 2, 3]]], dst=[[[0, 1]]]),
+                         "description": "Llama (hidden 64, ffn 8704) TP4 -> TP2 (shrink): 8704-byte fp32 rows joined"},
     "next_step": {"config": _cfg("next_step", NEXT_STEP_SPEC, src=[[[0, 1, 2, 3]]], dst=[[[0, 1]]]), "seed": 7,
                   "description": "small Llama TP4 -> TP2 with embeddings (shrink: the reference's cat order puts rank "
                                  "0's received pieces first, lm_head's vocab rows included); the state of the "

@@ -94,7 +94,7 @@ def test_views_move_only_row_split_pieces():
     assert info.total_bytes == moved + 4 * len([1 for r in (0, 1) for _ in out[r]])  # + one 4-byte step per tensor
 
 
-@pytest.mark.parametrize("variant", ["1", "2", "3", "4", "5", "6", "7", "8", "9", "10", "11", "12", "13", "14"])
+@pytest.mark.parametrize("variant", ["1", "2", "3", "4", "5", "6", "7", "8", "9", "10", "11", "12", "13", "14", "15"])
 @pytest.mark.parametrize("tile", ["256", "4096", "131072"])
 def test_copy_kernel_random_rectangles(tile, variant, monkeypatch):
     """Strided copies with random alignment, pitch and size (every vector width, column-split rows),
@@ -176,7 +176,7 @@ def test_stall_flag_needs_a_tma_shape(monkeypatch):
 
 @pytest.mark.parametrize("variant", ["9", "10", "11", "12", "13", "14"])
 def test_tensor_map_kernel_edges(variant, monkeypatch):
-    """The 2-D tensor-map kernel on the geometry its boxes have to clip: rows narrower than a box,
+    """The 3-D tensor-map kernel on the geometry its boxes have to clip: rows narrower than a box,
     widths that are not a multiple of the box width (odd element counts), row counts that leave a
     partial last box, one-row runs, and long contiguous runs cut into 2 KB rows plus a remainder.
     Every entry is local and 16-byte aligned, so all of them go to the tensor-map kernel."""
@@ -205,8 +205,40 @@ def test_tensor_map_kernel_edges(variant, monkeypatch):
     assert torch.equal(dst, want)
 
 
+def test_split_shape_gives_wide_rows_to_tensor_maps(monkeypatch):
+    """Launch shape 15: local, aligned slices wider than 8 KB and contiguous runs of 1 MB or more
+    take the tensor-map kernel; narrower slices, short runs and unaligned entries take the banded
+    vector copy, in the same run. Every target gets exactly its bytes."""
+    monkeypatch.setenv("SUIKA_RS_VARIANT", "15")
+    monkeypatch.delenv("SUIKA_RS_BAND_BYTES", raising=False)
+    g = torch.Generator(device=DEV).manual_seed(15)
+    src = torch.randint(0, 255, (64 << 20,), dtype=torch.uint8, device=DEV, generator=g)
+    dst = torch.zeros(64 << 20, dtype=torch.uint8, device=DEV)
+    want = torch.zeros_like(dst)
+    # (rows, row_bytes, src pitch, dst pitch, source offset misalignment, takes tensor maps)
+    shapes = [(700, 11008, 22016, 11008, 0, True), (300, 8192, 16384, 8192, 0, False), (1, 3 << 20, 0, 0, 0, True),
+              (1, 64 << 10, 0, 0, 0, False), (50, 16384, 32768, 16384, 8, False), (2048, 4096, 8192, 4096, 0, False),
+              (9, 40000, 80000, 40000, 0, True), (200, 4096, 4096, 4096, 0, False)]
+    descs, so, do, wide = [], 0, 0, 0
+    for rows, rb, sp, dp, mis, tma in shapes:
+        sp, dp = sp or rb, dp or rb
+        descs.append((src.data_ptr() + so + mis, dst.data_ptr() + do, rows, rb, sp, dp, 0))
+        want[do:do + rows * dp].view(rows, dp)[:, :rb] = src[so + mis:so + mis + rows * sp].view(rows, sp)[:, :rb]
+        wide += tma
+        so = (so + mis + rows * sp + 4095) // 4096 * 4096
+        do = (do + rows * dp + 4095) // 4096 * 4096
+    assert so <= src.numel() and do <= dst.numel()
+    prepared = M.PreparedCopies(np.array(descs, dtype=M.L.COPY_DESC_DTYPE), DEV)
+    info = prepared.launch()
+    assert info.variant == 14
+    assert info.n_tensor_entries >= wide and info.n_entries >= len(descs) - wide  # runs may add a remainder entry
+    torch.cuda.synchronize()
+    assert prepared.status() == 0
+    assert torch.equal(dst, want)
+
+
 @pytest.mark.parametrize("band", ["4096", "65536", "8388608"])
-@pytest.mark.parametrize("variant", ["2", "8", "9", "11", "12", "14"])
+@pytest.mark.parametrize("variant", ["2", "8", "9", "11", "12", "14", "15"])
 def test_groups_of_column_slices(variant, band, monkeypatch):
     """Column slices of the same source rows (the pieces of a TP grow by 2, 3, 4 and 8) are grouped:
     the vector copy cuts them into row bands of SUIKA_RS_BAND_BYTES and interleaves the bands, the
@@ -231,7 +263,9 @@ def test_groups_of_column_slices(variant, band, monkeypatch):
     table = np.array([descs[i] for i in rng.permutation(len(descs))], dtype=M.L.COPY_DESC_DTYPE)  # any table order
     prepared = M.PreparedCopies(table, DEV)
     info = prepared.launch()
-    if int(variant) >= 9:
+    if int(variant) == 15:  # slices wider than 8 KB (11008 and 40000 bytes) take tensor maps
+        assert info.n_tensor_entries == 4 and info.n_entries >= len(descs) - 4
+    elif int(variant) >= 9:
         assert info.n_entries == 0 and info.n_tensor_entries == len(descs)
     else:
         assert info.n_tensor_entries == 0 and info.n_entries >= len(descs)  # band-split entries
@@ -243,9 +277,10 @@ def test_groups_of_column_slices(variant, band, monkeypatch):
 @pytest.mark.parametrize("band", ["1024", "65536"])
 @pytest.mark.parametrize("case", ["cfg2b_mini", "grow_dp_tp_mini", "qwen_grow_mini", "cfg3_mini", "odd_mini", "next_step"])
 def test_reshard_local_band_interleaved_matches_reference(case, band, monkeypatch):
-    """The default one-GPU launch (vector copy, TP-grow slices cut into row bands and interleaved),
-    with bands small enough to cut the reduced-width golden cases, equals the reference's digests."""
-    monkeypatch.delenv("SUIKA_RS_VARIANT", raising=False)
+    """The vector copy of one-GPU tables (shape 8: TP-grow slices cut into row bands and
+    interleaved), with bands small enough to cut the reduced-width golden cases, equals the
+    reference's digests."""
+    monkeypatch.setenv("SUIKA_RS_VARIANT", "8")
     monkeypatch.setenv("SUIKA_RS_BAND_BYTES", band)
     g = load_golden(case)
     cfg = CASES[case]["config"]
@@ -264,18 +299,24 @@ def test_reshard_local_band_interleaved_matches_reference(case, band, monkeypatc
                 assert [list(t.shape), str(t.dtype).replace("torch.", ""), digest(host(t))] == exp, (rank_s, name, sub)
 
 
-@pytest.mark.parametrize("variant", ["9", "11", "14"])
-@pytest.mark.parametrize("case", ["cfg2b_mini", "cfg3_mini", "odd_mini", "qwen_grow_mini"])
+@pytest.mark.parametrize("variant", ["9", "11", "14", "15", "0"])
+@pytest.mark.parametrize("case", ["cfg2b_mini", "cfg3_mini", "odd_mini", "qwen_grow_mini", "wide_mini", "wide_shrink_mini"])
 def test_reshard_local_tensor_map_shapes_match_reference(case, variant, monkeypatch):
-    """A whole reshard through the tensor-map launch shapes equals the reference's digests."""
-    monkeypatch.setenv("SUIKA_RS_VARIANT", variant)
+    """A whole reshard through the tensor-map launch shapes equals the reference's digests ("0":
+    the default, shape 15; the wide cases give it rows for both of its kernels)."""
+    if variant == "0":
+        monkeypatch.delenv("SUIKA_RS_VARIANT", raising=False)
+    else:
+        monkeypatch.setenv("SUIKA_RS_VARIANT", variant)
     g = load_golden(case)
     cfg = CASES[case]["config"]
     spl, tpl = cfg.layouts()
     states = golden_states(cfg, seed=g["seed"])
-    out = M.reshard_local(spl, tpl, to_device(states), S.expected_sub_fields(), DEV,
-                          minimum_est_peers=g["minimum_est_peers"])
+    out, info, _ = M.reshard_local(spl, tpl, to_device(states), S.expected_sub_fields(), DEV,
+                                   minimum_est_peers=g["minimum_est_peers"], return_info=True)
     torch.cuda.synchronize()
+    if case.startswith("wide") and variant in ("0", "15"):
+        assert info.variant == 14 and info.n_tensor_entries > 0 and info.n_entries > 0  # both kernels ran
     for rank_s, want in g["ranks"].items():
         got = out[int(rank_s)]
         assert list(got) == want["order"]

@@ -39,7 +39,7 @@ def _tp_grow(k, rows, rb):
 
 def test_tp_grow_slices_are_cut_into_8_mb_bands(monkeypatch):
     monkeypatch.delenv("SUIKA_RS_BAND_BYTES", raising=False)
-    monkeypatch.delenv("SUIKA_RS_VARIANT", raising=False)
+    monkeypatch.setenv("SUIKA_RS_VARIANT", "8")
     info = _stage(_tp_grow(2, 4096, 22016))
     band_rows = (8 << 20) // 22016  # 381 rows per band
     bands = -(-4096 // band_rows)
@@ -56,14 +56,33 @@ def test_band_size_follows_the_setting(monkeypatch):
 def test_bands_shrink_to_fit_the_workspace(monkeypatch):
     """A workspace with room for 7 entries: the two slices get 3 bands each instead of 11."""
     monkeypatch.delenv("SUIKA_RS_BAND_BYTES", raising=False)
-    monkeypatch.delenv("SUIKA_RS_VARIANT", raising=False)
+    monkeypatch.setenv("SUIKA_RS_VARIANT", "8")
     info = _stage(_tp_grow(2, 4096, 22016), workspace_bytes=256 + 256 + 7 * 72)
     assert info.n_entries == 6
 
 
 def test_unrelated_entries_are_not_cut(monkeypatch):
     monkeypatch.delenv("SUIKA_RS_BAND_BYTES", raising=False)
-    monkeypatch.delenv("SUIKA_RS_VARIANT", raising=False)
+    monkeypatch.setenv("SUIKA_RS_VARIANT", "8")
     descs = [(BASE + i * (1 << 30), BASE + (1 << 36) + i * (1 << 30), 4096, 22016, 44032, 22016, 0) for i in range(3)]
     info = _stage(descs)  # same geometry, but each slice comes from its own source matrix
     assert info.n_entries == 3
+
+
+def test_default_one_gpu_shape_bands_its_narrow_rows(monkeypatch):
+    """Unset, a local table takes shape 15; its rows of 8 KB and less stay with the vector copy,
+    shape 8, and are cut into bands the same way (wide rows would go to the tensor-map kernel,
+    whose maps need a GPU to encode)."""
+    monkeypatch.delenv("SUIKA_RS_BAND_BYTES", raising=False)
+    monkeypatch.delenv("SUIKA_RS_VARIANT", raising=False)
+    info = _stage(_tp_grow(2, 4096, 8192))
+    band_rows = (8 << 20) // 8192  # 1024 rows per band
+    assert info.variant == 14 and info.n_tensor_entries == 0
+    assert info.n_entries == 2 * (4096 // band_rows)
+
+
+def test_remote_tables_keep_the_vector_shape(monkeypatch):
+    monkeypatch.delenv("SUIKA_RS_VARIANT", raising=False)
+    descs = [d[:6] + (L.RS_COPY_REMOTE,) for d in _tp_grow(2, 4096, 22016)]
+    info = _stage(descs)
+    assert info.variant == 1 and info.n_tensor_entries == 0 and info.n_entries == 2
