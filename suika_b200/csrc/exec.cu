@@ -11,8 +11,13 @@
 // of tile counts per entry, binary-searched by each CTA). CTAs stride over tiles; a CTA moves a
 // tile with 16-byte vector loads/stores (narrower only when an address or pitch is not 16-byte
 // aligned), several loads in flight per thread before their stores, which keeps enough bytes
-// outstanding to cover NVLink read latency as well as HBM latency. The copy is pure data
-// movement: no tensor cores, no TMA multicast (this code runs on several GPUs), no waits.
+// outstanding to cover NVLink read latency as well as HBM latency.
+//
+// Two TMA kernels run the same tables: a bulk copy (cp.async.bulk, one request per row) and a
+// tensor-map copy (cp.async.bulk.tensor.3d boxes of whole rows) that takes the wide local rows of
+// a one-GPU relayout. The copy is pure data movement: no tensor cores, and no TMA multicast (this
+// code runs on several GPUs). The vector kernel has no waits; the TMA kernels' mbarrier waits are
+// bounded by %globaltimer and report a timeout in the table's status word.
 #include "../../include/suika_reshard.h"
 #include "internal.h"
 
