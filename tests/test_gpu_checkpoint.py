@@ -19,7 +19,7 @@ DEV = torch.device("cuda", 0)
 
 @pytest.mark.parametrize("case", ["cfg1", "cfg2_mini", "cfg2_mini_noib", "cfg3_mini", "cfg4_mini", "cfg5_mini",
                                   "shrink_mini", "hetero_mini", "odd_mini", "pp_deepen_mini", "gpt_shrink_mini",
-                                  "grow_dp_tp_mini", "qwen_grow_mini"])
+                                  "grow_dp_tp_mini", "qwen_grow_mini", "wide_mini", "wide_shrink_mini"])
 def test_checkpoint_resume_matches_reference(case, monkeypatch):
     g = load_golden(case)
     if g["minimum_est_peers"] == 2:

@@ -75,7 +75,7 @@ def run_case(case, port, directions=("pull", "push")):
 
 @pytest.mark.parametrize("case", ["cfg2b_mini", "odd_mini", "cfg1", "cfg2_mini", "cfg3_mini", "cfg4_mini", "cfg5_mini",
                                   "shrink_mini", "hetero_mini", "cfg2_mini_noib", "pp_deepen_mini", "gpt_shrink_mini",
-                                  "grow_dp_tp_mini", "qwen_grow_mini"])
+                                  "grow_dp_tp_mini", "qwen_grow_mini", "wide_mini", "wide_shrink_mini", "next_step"])
 def test_drop_in_matches_reference(case):
     """Pull, then push, in the same processes; both against the reference's digests."""
     g = load_golden(case)
