@@ -267,7 +267,7 @@ typedef struct rs_launch_info {
   int32_t block;           /* threads per CTA                          */
   int32_t variant;         /* launch shape (SUIKA_RS_VARIANT - 1)      */
   int32_t reserved;
-  /* Tensor-map launch shapes (SUIKA_RS_VARIANT 9-15): the local, 16-byte aligned entries go to a
+  /* Tensor-map launch shapes (SUIKA_RS_VARIANT 9-17): the local, 16-byte aligned entries go to a
    * kernel that moves 3-D boxes with cp.async.bulk.tensor (one load and one store per box of
    * whole rows, or up to 2 KB x rows); the fields above then describe the other entries, run by
    * the vector copy. */
@@ -283,10 +283,10 @@ typedef struct rs_launch_info {
 int rs_copy_workspace_bytes(int64_t n_desc, uint64_t* bytes);
 /* Cut the table into tiles and stage it into workspace_dev (stream-ordered copy on `stream`, a
  * cudaStream_t; NULL = legacy default stream). Fills *info for rs_copy_run. The launch shape is
- * SUIKA_RS_VARIANT's; unset, a table with no RS_COPY_REMOTE entry takes shape 15 and any other
- * table the vector shape 2. Shape 15 gives the local, 16-byte aligned entries with rows wider than
- * 8 KB, and contiguous runs of 1 MB or more, to the tensor-map kernel, and the rest to the vector
- * shape 8, in the same run. For the vector shapes, local entries that are column slices of the
+ * SUIKA_RS_VARIANT's; unset, a table with no RS_COPY_REMOTE entry takes shape 17 and any other
+ * table the vector shape 2. Shapes 15-17 give the local, 16-byte aligned entries with rows wider
+ * than 8 KB, and contiguous runs of 1 MB or more, to the tensor-map kernel (17: 3 x 72 KB stages),
+ * and the rest to the vector shape 8, in the same run. For the vector shapes, local entries that are column slices of the
  * same source rows (a TP grow's pieces) are cut into row bands of about SUIKA_RS_BAND_BYTES
  * (default 8 MB) per slice and interleaved, so that whole source rows are read at once;
  * rs_launch_info.n_entries counts the entries after that cut. */

@@ -495,7 +495,7 @@ __global__ void __launch_bounds__(32, MINB) rs_copy_tma_kernel(const DevSeg* __r
 }
 
 // ---------------------------------------------------------------------------------------------
-// Tensor-map variant: TMA boxes through a shared-memory ring (SUIKA_RS_VARIANT 9-15).
+// Tensor-map variant: TMA boxes through a shared-memory ring (SUIKA_RS_VARIANT 9-17).
 // Every local, 16-byte aligned entry is described to the TMA unit as two tensors of 8-byte
 // elements, its source and its target, each its rows with their own pitch; one
 // cp.async.bulk.tensor.3d load moves a box (whole rows, or a 2 KB-wide strided tile) into a
@@ -698,7 +698,7 @@ const Variant kVariants[] = {
     {256, 8, 2, 0, rs_copy_kernel<256, 8, 2, true>},  // 8: variant 2 with streaming cache hints
 };
 constexpr int kNumVariants = sizeof(kVariants) / sizeof(kVariants[0]);
-// Tensor-map launch shapes (SUIKA_RS_VARIANT 9-15): (stages, stage bytes, evict-first hints); one warp per CTA, CTAs
+// Tensor-map launch shapes (SUIKA_RS_VARIANT 9-17): (stages, stage bytes, evict-first hints); one warp per CTA, CTAs
 // per SM as shared memory allows (1 for about 192 KB of stages, 2 for about 96 KB). `vector` is the
 // launch shape of the entries the tensor-map kernel leaves out; `wide_only` keeps it to the rows it
 // reads fastest (wide_desc), leaving the narrower ones to the banded vector copy.
@@ -717,7 +717,11 @@ const TensorShape kTensorShapes[] = {
     {8, 24576, tensor_smem_bytes<8, 24576>(), rs_copy_tensor_kernel<8, 24576, true>, 1, false},  // 13: 9 with evict-first L2 hints
     {4, 49152, tensor_smem_bytes<4, 49152>(), rs_copy_tensor_kernel<4, 49152, true>, 1, false},  // 14: 11 with evict-first L2 hints
     {4, 49152, tensor_smem_bytes<4, 49152>(), rs_copy_tensor_kernel<4, 49152, false>, 7, true},  // 15: 11 for wide rows, 8 for the rest
+    {4, 57344, tensor_smem_bytes<4, 57344>(), rs_copy_tensor_kernel<4, 57344, false>, 7, true},  // 16: 15 with 56 KB stages
+    {3, 73728, tensor_smem_bytes<3, 73728>(), rs_copy_tensor_kernel<3, 73728, false>, 7, true},  // 17: 15 with 3 x 72 KB stages
 };
+static_assert(tensor_smem_bytes<4, 57344>() <= 232448 && tensor_smem_bytes<3, 73728>() <= 232448,
+              "a tensor-map shape exceeds 227 KB of shared memory per CTA");
 constexpr int kNumTensorShapes = sizeof(kTensorShapes) / sizeof(kTensorShapes[0]);
 
 // Workspace layout: the staged vector-copy table, a 256-byte status block (word 0: kStatus* bits),
@@ -737,13 +741,14 @@ uint64_t env_u64(const char* name, uint64_t dflt) {
 
 // Launch shape chosen by SUIKA_RS_VARIANT (1-based): 0-based index below kNumVariants for the
 // vector and bulk-copy kernels, kNumVariants + i for tensor-map shape i. Unset (or 0) selects per
-// table: a table whose entries all stay in this GPU's memory runs shape 15 (wide rows and long
-// runs through the tensor-map kernel, the other rows through the vector shape 8 with evict-first
-// stores and band-interleaved TP-grow slices: the fastest split on a one-GPU relayout); a table
+// table: a table whose entries all stay in this GPU's memory runs shape 17 (wide rows and long
+// runs through the tensor-map kernel with 3 x 72 KB stages, the other rows through the vector
+// shape 8 with evict-first stores and band-interleaved TP-grow slices: the fastest split on a
+// one-GPU relayout); a table
 // with any entry that crosses NVLink, or reads host memory, runs the vector shape 2, whose CTAs
 // interleave remote and local tiles so both links stay busy.
 constexpr int kAutoVariant = -1;
-constexpr int kAutoLocalVariant = 14;  // kNumVariants + 6: tensor-map shape 15
+constexpr int kAutoLocalVariant = 16;  // kNumVariants + 8: tensor-map shape 17
 constexpr int kAutoRemoteVariant = 1;
 int selected_variant() {
   const uint64_t v = env_u64("SUIKA_RS_VARIANT", 0);
@@ -1178,7 +1183,7 @@ int rs_copy_run_bounded(const void* workspace_dev, const rs_launch_info* info, v
   const bool tensor = is_tensor_variant(info->variant);
   const Variant& v = kVariants[vector_variant_of(info->variant)];
   if ((flags & RS_RUN_STALL_FIRST_STAGE) && !(tensor ? tensor_part : v.smem > 0))
-    return efail(RS_ERR_ARG, "rs_copy_run_bounded: RS_RUN_STALL_FIRST_STAGE needs a TMA launch shape (SUIKA_RS_VARIANT 5-7 or 9-15)");
+    return efail(RS_ERR_ARG, "rs_copy_run_bounded: RS_RUN_STALL_FIRST_STAGE needs a TMA launch shape (SUIKA_RS_VARIANT 5-7 or 9-17)");
   char* ws = static_cast<char*>(const_cast<void*>(workspace_dev));
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   RunArgs run;

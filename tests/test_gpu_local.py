@@ -94,7 +94,8 @@ def test_views_move_only_row_split_pieces():
     assert info.total_bytes == moved + 4 * len([1 for r in (0, 1) for _ in out[r]])  # + one 4-byte step per tensor
 
 
-@pytest.mark.parametrize("variant", ["1", "2", "3", "4", "5", "6", "7", "8", "9", "10", "11", "12", "13", "14", "15"])
+@pytest.mark.parametrize("variant", ["1", "2", "3", "4", "5", "6", "7", "8", "9", "10", "11", "12", "13", "14", "15", "16",
+                                     "17"])
 @pytest.mark.parametrize("tile", ["256", "4096", "131072"])
 def test_copy_kernel_random_rectangles(tile, variant, monkeypatch):
     """Strided copies with random alignment, pitch and size (every vector width, column-split rows),
@@ -238,7 +239,7 @@ def test_split_shape_gives_wide_rows_to_tensor_maps(monkeypatch):
 
 
 @pytest.mark.parametrize("band", ["4096", "65536", "8388608"])
-@pytest.mark.parametrize("variant", ["2", "8", "9", "11", "12", "14", "15"])
+@pytest.mark.parametrize("variant", ["2", "8", "9", "11", "12", "14", "15", "16", "17"])
 def test_groups_of_column_slices(variant, band, monkeypatch):
     """Column slices of the same source rows (the pieces of a TP grow by 2, 3, 4 and 8) are grouped:
     the vector copy cuts them into row bands of SUIKA_RS_BAND_BYTES and interleaves the bands, the
@@ -263,7 +264,7 @@ def test_groups_of_column_slices(variant, band, monkeypatch):
     table = np.array([descs[i] for i in rng.permutation(len(descs))], dtype=M.L.COPY_DESC_DTYPE)  # any table order
     prepared = M.PreparedCopies(table, DEV)
     info = prepared.launch()
-    if int(variant) == 15:  # slices wider than 8 KB (11008 and 40000 bytes) take tensor maps
+    if int(variant) >= 15:  # slices wider than 8 KB (11008 and 40000 bytes) take tensor maps
         assert info.n_tensor_entries == 4 and info.n_entries >= len(descs) - 4
     elif int(variant) >= 9:
         assert info.n_entries == 0 and info.n_tensor_entries == len(descs)
@@ -303,7 +304,7 @@ def test_reshard_local_band_interleaved_matches_reference(case, band, monkeypatc
 @pytest.mark.parametrize("case", ["cfg2b_mini", "cfg3_mini", "odd_mini", "qwen_grow_mini", "wide_mini", "wide_shrink_mini"])
 def test_reshard_local_tensor_map_shapes_match_reference(case, variant, monkeypatch):
     """A whole reshard through the tensor-map launch shapes equals the reference's digests ("0":
-    the default, shape 15; the wide cases give it rows for both of its kernels)."""
+    the default, shape 17; the wide cases give the split shapes rows for both of their kernels)."""
     if variant == "0":
         monkeypatch.delenv("SUIKA_RS_VARIANT", raising=False)
     else:
@@ -316,7 +317,8 @@ def test_reshard_local_tensor_map_shapes_match_reference(case, variant, monkeypa
                                    minimum_est_peers=g["minimum_est_peers"], return_info=True)
     torch.cuda.synchronize()
     if case.startswith("wide") and variant in ("0", "15"):
-        assert info.variant == 14 and info.n_tensor_entries > 0 and info.n_entries > 0  # both kernels ran
+        assert info.variant == (16 if variant == "0" else 14)
+        assert info.n_tensor_entries > 0 and info.n_entries > 0  # both kernels ran
     for rank_s, want in g["ranks"].items():
         got = out[int(rank_s)]
         assert list(got) == want["order"]

@@ -70,14 +70,14 @@ def test_unrelated_entries_are_not_cut(monkeypatch):
 
 
 def test_default_one_gpu_shape_bands_its_narrow_rows(monkeypatch):
-    """Unset, a local table takes shape 15; its rows of 8 KB and less stay with the vector copy,
+    """Unset, a local table takes shape 17; its rows of 8 KB and less stay with the vector copy,
     shape 8, and are cut into bands the same way (wide rows would go to the tensor-map kernel,
     whose maps need a GPU to encode)."""
     monkeypatch.delenv("SUIKA_RS_BAND_BYTES", raising=False)
     monkeypatch.delenv("SUIKA_RS_VARIANT", raising=False)
     info = _stage(_tp_grow(2, 4096, 8192))
     band_rows = (8 << 20) // 8192  # 1024 rows per band
-    assert info.variant == 14 and info.n_tensor_entries == 0
+    assert info.variant == 16 and info.n_tensor_entries == 0
     assert info.n_entries == 2 * (4096 // band_rows)
 
 
