@@ -235,12 +235,13 @@ def cpu_baseline_block(cfg, n_gpus, threads, budget_s=20.0):
 
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per moved byte of the one-GPU pack
-# (default launch shape 15: the banded vector copy and the tensor-map copy, one launch each per
-# step), from one ncu capture of both launches of one step on a 2-layer cfg2b case (1.732 GB moved
-# per step, above L2): `ncu --set full --clock-control none -k regex:rs_copy -s 8 -c 2 python
-# bench.py --layers 2 --steps 3 --warmup 3 --no-e2e --no-cpu-baseline --no-check` gave 0.470 +
-# 1.263 GB read and 0.419 + 1.221 GB written. Traffic grows with the moved bytes (every byte is
-# read once and written once), so a full step's traffic is this ratio x moved.
+# (the split launch: the banded vector copy and the tensor-map copy, one launch each per step),
+# from one ncu capture of both launches of one step on a 2-layer cfg2b case (1.732 GB moved per
+# step, above L2), taken with shape 15 as the default: `ncu --set full --clock-control none -k
+# regex:rs_copy -s 8 -c 2 python bench.py --layers 2 --steps 3 --warmup 3 --no-e2e
+# --no-cpu-baseline --no-check` gave 0.470 + 1.263 GB read and 0.419 + 1.221 GB written. Shape 17
+# (the default now) moves the same rows with larger boxes, each byte again read once and written
+# once. Traffic grows with the moved bytes, so a full step's traffic is this ratio x moved.
 DRAM_BYTES_PER_MOVED_BYTE = 1.947
 
 
