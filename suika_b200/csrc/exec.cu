@@ -748,8 +748,10 @@ uint64_t env_u64(const char* name, uint64_t dflt) {
 // with any entry that crosses NVLink, or reads host memory, runs the vector shape 2, whose CTAs
 // interleave remote and local tiles so both links stay busy.
 constexpr int kAutoVariant = -1;
-constexpr int kAutoLocalVariant = 16;  // kNumVariants + 8: tensor-map shape 17
+constexpr int kAutoLocalVariant = kNumVariants + 8;  // tensor-map shape 17 (SUIKA_RS_VARIANT=17)
 constexpr int kAutoRemoteVariant = 1;
+static_assert(kAutoLocalVariant == 16 && kAutoLocalVariant < kNumVariants + kNumTensorShapes,
+              "the one-GPU default must be a tensor-map shape");
 int selected_variant() {
   const uint64_t v = env_u64("SUIKA_RS_VARIANT", 0);
   if (v == 0) return kAutoVariant;
