@@ -86,3 +86,17 @@ def test_remote_tables_keep_the_vector_shape(monkeypatch):
     descs = [d[:6] + (L.RS_COPY_REMOTE,) for d in _tp_grow(2, 4096, 22016)]
     info = _stage(descs)
     assert info.variant == 1 and info.n_tensor_entries == 0 and info.n_entries == 2
+
+
+@pytest.mark.parametrize("variant", ["15", "16", "17"])
+def test_split_shapes_band_narrow_rows_like_shape_8(variant, monkeypatch):
+    """The split shapes hand rows of 8 KB and less to the vector copy, cut into the same bands as
+    shape 8 gives them, and leave the tensor-map part empty."""
+    monkeypatch.delenv("SUIKA_RS_BAND_BYTES", raising=False)
+    monkeypatch.setenv("SUIKA_RS_VARIANT", "8")
+    want = _stage(_tp_grow(4, 8192, 4096))
+    monkeypatch.setenv("SUIKA_RS_VARIANT", variant)
+    info = _stage(_tp_grow(4, 8192, 4096))
+    assert info.variant == int(variant) - 1 and info.n_tensor_entries == 0
+    assert (info.n_entries, info.n_tiles, info.total_bytes) == (want.n_entries, want.n_tiles, want.total_bytes)
+    assert info.n_entries == 16  # four 8 MB bands per 32 MB slice
