@@ -1344,30 +1344,40 @@ def execute_from_host(plan: Plan, rank: int, source_state_dict, fake_source_stat
     # every chunk's table is staged before the gather starts, so a chunk's launch is a kernel launch only
     chunks = [PreparedCopies(table[seg_chunk == k], device) if np.any(seg_chunk == k) else None for k in range(n_chunks)]
     launched = []
-    for k in range(n_chunks):
-        for i in np.nonzero(chunk_of == k)[0]:
-            o, n = int(off[i]), int(nb[i])
-            arena[o:o + n].copy_(hs[i].reshape(-1).view(torch.uint8))
-        if chunks[k] is not None:
-            chunks[k].launch()
-            launched.append(chunks[k])
-    ent: Dict[str, Dict[str, torch.Tensor]] = {}
-    for ds, x in zip(prog.dst_slots, dst_t):
-        ent.setdefault(plan.names[ds["name_id"]], {})[subs[ds["subfield"]]] = x
-    meta = _MetaStage(device)
-    for ms in prog.meta_slots:
-        name, s = plan.names[int(ms["name_id"])], subs[int(ms["subfield"])]
-        v = host_src(int(ms["src_rank"]), name, s)
-        x = torch.empty(v.shape, dtype=v.dtype, device=device)
-        meta.add(v, x)
-        ent.setdefault(name, {})[s] = x
-    md, stage = meta.descs()
-    if len(md):
-        p = PreparedCopies(md, device)
-        p.launch()
-        launched.append(p)
-    for p in launched:
-        p.check()  # synchronises: the arena and the staging buffer may go after this
+    try:
+        for k in range(n_chunks):
+            for i in np.nonzero(chunk_of == k)[0]:
+                o, n = int(off[i]), int(nb[i])
+                arena[o:o + n].copy_(hs[i].reshape(-1).view(torch.uint8))
+            if chunks[k] is not None:
+                chunks[k].launch()
+                launched.append(chunks[k])
+        ent: Dict[str, Dict[str, torch.Tensor]] = {}
+        for ds, x in zip(prog.dst_slots, dst_t):
+            ent.setdefault(plan.names[ds["name_id"]], {})[subs[ds["subfield"]]] = x
+        meta = _MetaStage(device)
+        for ms in prog.meta_slots:
+            name, s = plan.names[int(ms["name_id"])], subs[int(ms["subfield"])]
+            v = host_src(int(ms["src_rank"]), name, s)
+            x = torch.empty(v.shape, dtype=v.dtype, device=device)
+            meta.add(v, x)
+            ent.setdefault(name, {})[s] = x
+        md, stage = meta.descs()
+        if len(md):
+            p = PreparedCopies(md, device)
+            p.launch()
+            launched.append(p)
+        for p in launched:
+            p.check()  # synchronises: the arena and the staging buffer may go after this
+    except BaseException:
+        # the kernels read the arena through a device pointer the pinned-memory cache does not
+        # track: none of them may still be reading it when it goes back to the cache
+        if launched:
+            try:
+                torch.cuda.synchronize(device)
+            except Exception:
+                pass
+        raise
     del arena, stage
     return {plan.names[n]: {s: ent[plan.names[n]][s] for s in subs if s in ent[plan.names[n]]} for n in _name_order(plan, rank)}
 
