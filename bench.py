@@ -492,8 +492,10 @@ def run_dist(args):
         torch.cuda.synchronize()
         dist.barrier()
     per_rank = [None] * world
-    dist.all_gather_object(per_rank, (round(statistics.mean(kern), 4), int(rt.remote_bytes), int(rt.local_bytes),
-                                      sum(1 for p in rt.prepared_phases if p is not None)))
+    # kernels per step on this rank: one per phase, two where a phase's table is split between the
+    # vector and the tensor-map kernel (a phase with only local pieces, under the default shape)
+    n_launch = sum(int(p.info.n_entries > 0) + int(p.info.n_tensor_entries > 0) for p in rt.prepared_phases if p is not None)
+    dist.all_gather_object(per_rank, (round(statistics.mean(kern), 4), int(rt.remote_bytes), int(rt.local_bytes), n_launch))
     rt_phase_counts = [p[3] for p in per_rank]
     t = max(p[0] for p in per_rank) / 1e3  # the step ends when the slowest rank's kernel ends
     check = verify_dist(plan, rt, rank, state.state, exp) if not args.no_check else {"status": "skipped"}
